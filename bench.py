@@ -1,0 +1,317 @@
+#!/usr/bin/env python
+"""AR decode benchmark: tokens/s of YuE2's CFG decode loop on B200.
+
+Product arm (default): BASELINE config 1 -- the 3B-shaped AR model (28 layers, hidden
+3072, 24/8 heads, intermediate 8192, vocab 84,000, synthetic bf16 N(0, 0.02) weights,
+seed 1), CFG on (scale 1.5), 1,024-id cond and uncond prompts, sampling T 1.0 / top-k 50 /
+top-p 0.93. One step = one decode token: both CFG rows through every layer in one weight
+pass, LM head, on-device CFG mix + choose (one CUDA-graph launch). W untimed steps, then
+K timed steps between barriers; time = CUDA events on the decode stream, max over ranks.
+Data-parallel over songs: every rank runs its own song (weak scaling, no collective).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+`--impl reference` times the reference's CPU decode math (the scalar host build in
+oracle/, all host threads) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "AR decode tokens/s/GPU (CFG, 4k & 24k ctx) and % of HBM roofline; 1/2/4/8 GPU"
+UNIT = "tokens/s"
+PROMPT = 1024
+SCALE = 1.5
+
+
+def c2_sampling(max_tokens):
+    from yue2_rs_b200 import Sampling
+    # config 1: T 1.0, top-k 50, top-p 0.93; repetition penalty 1.0 (window 50), min_tokens 0
+    return Sampling(1.0, 0.93, 50, 1.0, 50, 0, max_tokens)
+
+
+def prompts(seed, vocab):
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, vocab, PROMPT).tolist(), rng.integers(0, vocab, PROMPT).tolist()
+
+
+def weight_bytes(c):
+    H, I, V, D = c.hidden_size, c.intermediate_size, c.vocab_size, c.head_dim
+    qd, kd = c.num_attention_heads * D, c.num_key_value_heads * D
+    per_layer = 2 * (qd * H + 2 * kd * H + H * qd + 3 * I * H)
+    return c.num_hidden_layers * per_layer + V * H * 2 + (2 * c.num_hidden_layers + 1) * H * 2
+
+
+def kv_bytes_per_token(c):
+    return c.num_hidden_layers * 2 * c.num_key_value_heads * c.head_dim * 2
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) of this rank's GPU during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait(timeout=10)
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(config, steps_budget_s=20.0, threads=None):
+    """The oracle (scalar host build of the reference's decode math) on the host cores:
+    the config-1 decode step (two forwards -- cond and uncond, as sampling.rs:281-285
+    runs them -- CFG mix and choose) at a 1,024-position synthetic context, timed for
+    about `steps_budget_s` seconds."""
+    from oracle import oracle as orc
+    from yue2_rs_b200 import Phase
+    if threads:
+        orc.set_threads(threads)
+    cores = orc.lib().orc_max_threads()
+    t0 = time.perf_counter()
+    m = orc.OracleModel.synthetic(config, seed=1, std=0.02)
+    setup = time.perf_counter() - t0
+    c = config
+    kvw = c.num_key_value_heads * c.head_dim
+    rng = np.random.default_rng(0)
+    caches = []
+    for side in range(2):
+        bits = (rng.standard_normal((c.num_hidden_layers, 2, PROMPT, kvw), dtype=np.float32).view(np.uint32) >> 16)
+        oc = m.cache(PROMPT + 64)
+        oc.write(PROMPT, bits.astype(np.uint16))
+        caches.append(oc)
+    s = c2_sampling(64)
+    g = orc.OracleRng(1)
+    tok, toks, n = 0, [], 0
+    t0 = time.perf_counter()
+    while True:
+        lc = m.forward([tok], caches[0])
+        lu = m.forward([tok], caches[1])
+        tok = orc.choose(orc.cfg_mix(lc, lu, SCALE), s, toks, n, int(Phase.VOCAB), False, g)
+        toks.append(tok)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= steps_budget_s or n >= 60:
+            break
+    m.close()
+    return {"value": n / el, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} config-1 decode tokens (2 forwards + CFG mix + choose each) at a 1,024-position "
+                      f"synthetic context; weights seeded N(0,0.02) (setup {setup:.1f}s untimed); scalar host build "
+                      f"of the reference decode math, not Accelerate"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from yue2_rs_b200 import synth
+    cb = cpu_baseline(synth.config_c2(), steps_budget_s=max(5.0, min(25.0, 3.0 * args.steps)))
+    line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config 1: 3B-shaped AR decode, CFG 1.5, T1.0/top-k50/top-p0.93, 1,024 ctx",
+                       "parallelism": "host threads"},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="product", choices=["product", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from yue2_rs_b200 import Model, Phase, Request, Session, generate_batch, synth, _lib
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = synth.config_c2()
+    model = Model.synthetic(cfg, seed=1, std=0.02, device=local)
+    W, K = max(args.warmup, 3), args.steps
+    max_tokens = max(512, W + K + 1)
+    cond, uncond = prompts(1000 + rank, cfg.vocab_size)
+    s = c2_sampling(max_tokens)
+
+    # ---- device-resident timed region: K decode steps of one song per rank
+    sess = Session(model, [Request(cond, seed=rank, negative=uncond, scale=SCALE)], s, Phase.VOCAB)
+    stream = torch.cuda.ExternalStream(sess.cuda_stream)
+    sess.step(W)
+    sess.sync()
+    barrier()
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    launched = sess.step(K)
+    e1.record(stream)
+    sess.sync()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    assert launched == K, launched
+    kps = sess.kernels_per_step
+    toks, _ = sess.collect()[0]
+    assert len(toks) == W + K + 1
+    sess.close()
+    value = world * K / (ms / 1000.0)
+    ctx_avg = PROMPT + 1 + W + K / 2.0
+    step_bytes = weight_bytes(cfg) + 2 * kv_bytes_per_token(cfg) * ctx_avg
+    peak, peak_kind = measured_peaks()
+
+    # ---- dominant kernel live: the gate|up GEMV (fused RMSNorm prologue + SwiGLU epilogue)
+    import ctypes
+    avg = ctypes.c_double()
+    per = ctypes.c_double()
+    _lib.check(_lib.lib().yue2_bench_gemv(model._h, 0, 2, 10 * cfg.num_hidden_layers, ctypes.byref(avg),
+                                          ctypes.byref(per)))
+    kern_gbs = per.value / (avg.value * 1e-3) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "gemv_gateup_c2_traffic.json")
+    if os.path.exists(prof):
+        with open(prof) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+
+    # ---- long-context sweep (config 2): decode at 4,096 and 24,576 positions
+    sweep = {}
+    if not args.no_sweep:
+        for L in (4096, 24576):
+            ks = 32
+            mt = 4 + ks + 1
+            fill = L - 8 - mt - 1 if L == 24576 else L - 8
+            r = Request(cond[:8], seed=rank, negative=uncond[:8], scale=SCALE, context_fill=fill)
+            ss = Session(model, [r], c2_sampling(mt), Phase.VOCAB)
+            st = torch.cuda.ExternalStream(ss.cuda_stream)
+            ss.step(4)
+            ss.sync()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            ss.step(ks)
+            b.record(st)
+            ss.sync()
+            barrier()
+            sms = max_over_ranks(a.elapsed_time(b))
+            ss.close()
+            ctx = fill + 8 + 5 + ks / 2.0
+            sb = weight_bytes(cfg) + 2 * kv_bytes_per_token(cfg) * ctx
+            sweep[str(L)] = {"tokens_per_s": world * ks / (sms / 1000.0), "ms_per_step": sms / ks,
+                             "context_mid": ctx, "step_bytes": sb,
+                             "hbm_frac_of_measured": sb / (sms / ks * 1e-3) / 1e9 / peak,
+                             "hbm_frac_of_8TBs": sb / (sms / ks * 1e-3) / 8e12}
+
+    # ---- end to end through the public C ABI with host buffers (prefill included)
+    barrier()
+    t0 = time.perf_counter()
+    outs = generate_batch(model, [Request(cond, seed=rank + 7, negative=uncond, scale=SCALE)], c2_sampling(512),
+                          Phase.VOCAB)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_tokens = len(outs[0].tokens) * world
+    h2d = 2 * PROMPT * 4
+    d2h = 512 * 4
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,0.02) bf16 weights, uniform random prompt ids",
+        "config": {"workload": "config 1: 3B-shaped AR decode (28L, H3072, 24/8 heads, I8192, V84000), CFG 1.5, "
+                               "T1.0 top-k50 top-p0.93, 1,024-id cond+uncond prompts",
+                   "global_batch": world, "context": f"{PROMPT + W + 1}..{PROMPT + W + K + 1}",
+                   "parallelism": f"dp{world} (one song per GPU, no collective)",
+                   "l2": "inputs larger than L2: 6.15 GB of weights streamed per step (126 MB L2), no flush",
+                   "phase": "vocabulary-generic choose (vocab 84,000 has no codec window)"},
+        "gpu_launches": kps * K,
+        "clocks": clk,
+        "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s", "frac": kern_gbs / peak,
+                     "traffic": traffic, "kernel": "gemv gate|up + SwiGLU, 2 rows (CFG), 100.7 MB per launch",
+                     "peak_kind": peak_kind},
+        "step_roofline": {"step_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
+                          "frac_of_measured": step_bytes / (ms / K * 1e-3) / 1e9 / peak,
+                          "frac_of_8TBs": step_bytes / (ms / K * 1e-3) / 8e12},
+        "ctx_sweep": sweep,
+        "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "what": "yue2_generate: 512 tokens per song incl. both 1,024-id prefills, host buffers in/out"},
+    }
+    model.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,47 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) GPU; compares the CUDA path with the oracle")
+
+
+@pytest.fixture(scope="session")
+def c1_config():
+    from yue2_rs_b200 import synth
+    return synth.config_c1()
+
+
+@pytest.fixture(scope="session")
+def c1_dir(tmp_path_factory, c1_config):
+    """the reduced model as a safetensors checkpoint (seed 0)."""
+    from yue2_rs_b200 import synth
+    return synth.write_checkpoint(str(tmp_path_factory.mktemp("c1")), c1_config, seed=0)
+
+
+@pytest.fixture(scope="session")
+def c1_oracle(c1_dir, c1_config):
+    from oracle.oracle import OracleModel
+    from yue2_rs_b200 import checkpoint
+    return OracleModel.from_tensors(c1_config, checkpoint.tensors(c1_dir))
+
+
+@pytest.fixture(scope="session")
+def c1_device(c1_dir):
+    from yue2_rs_b200 import Model
+    return Model.open(c1_dir)
+
+
+@pytest.fixture(scope="session")
+def c1_prompt(c1_config):
+    """256 token ids uniform over the vocabulary (seeded) and 64 teacher-forced ids."""
+    rng = np.random.default_rng(12345)
+    return (rng.integers(0, c1_config.vocab_size, 256).tolist(), rng.integers(0, c1_config.vocab_size, 64).tolist())

@@ -1,0 +1,72 @@
+"""sm_100a split-K decode attention through the drop-in yue2_cuda_cached_attention
+(metal.m:686-706) against the reference's golden test (src/tensor.rs:7-83)."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from golden.make_golden import attention_inputs
+from yue2_rs_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "attention_ref.npz")
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def test_device_present():
+    assert _lib.lib().yue2_cuda_available() == 1, _lib.last_error()
+
+
+@pytest.mark.parametrize("dim", [64, 128, 256])
+def test_cached_attention_matches_reference_golden(dim):
+    L = _lib.lib()
+    heads, kv, cache = 4, 2, 9000 + dim
+    golden = np.load(GOLDEN)
+    for keys in (4096, 4097, 7169, 24576):
+        for append in (0, 1) if keys < 24576 else (0,):
+            q, k, v = attention_inputs(heads, kv, dim, keys, append)
+            out = np.empty(heads * dim, dtype=np.float32)
+            ok = L.yue2_cuda_cached_attention(_p(q), _p(k), _p(v), _p(out), k.shape[0], heads, kv, dim, cache, 0)
+            assert ok == 1, _lib.last_error()
+            want = golden[f"d{dim}_k{keys}_a{append}"]
+            err = np.abs(out - want)
+            assert np.all(err <= 5e-5 + np.abs(want) * 0.008), (keys, append, float(err.max()))
+    L.yue2_cuda_release_cache(cache)
+
+
+def test_attention_short_contexts_against_oracle():
+    from oracle.oracle import attention
+    L = _lib.lib()
+    rng = np.random.default_rng(3)
+    for keys in (1, 2, 31, 32, 33, 63, 64, 65, 200, 1000):
+        heads, kv, dim = 24, 8, 128
+        to_bf = lambda a: (a.astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
+        q = to_bf(rng.standard_normal(heads * dim))
+        k = to_bf(rng.standard_normal((keys, kv * dim)))
+        v = to_bf(rng.standard_normal((keys, kv * dim)))
+        out = np.empty(heads * dim, dtype=np.float32)
+        assert L.yue2_cuda_cached_attention(_p(q), _p(k), _p(v), _p(out), keys, heads, kv, dim, 77, 1) == 1
+        want = attention(q, k, v, heads, kv, dim)
+        assert np.all(np.abs(out - want) <= 5e-5 + np.abs(want) * 0.008), keys
+        L.yue2_cuda_release_cache(77)
+
+
+def test_vector_dropin_matches_f64():
+    L = _lib.lib()
+    rng = np.random.default_rng(5)
+    for rows, cols in ((1024, 3072), (3072, 8192), (333, 1024)):
+        w = (rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+        wb = (w.view(np.uint32) >> 16).astype(np.uint16)
+        wf = (wb.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        x = rng.standard_normal(cols).astype(np.float32)
+        out = np.empty(rows, dtype=np.float32)
+        ok = L.yue2_cuda_vector(_p(x), _p(wb), 1234, 0, 1, 1, _p(out), rows, cols)
+        assert ok == 1, _lib.last_error()
+        want = wf @ x.astype(np.float64)
+        scale = np.abs(wf) @ np.abs(x.astype(np.float64))
+        assert np.all(np.abs(out - want) <= 1e-5 * scale + 1e-6)
+    L.yue2_cuda_clear_weights()

@@ -1,0 +1,71 @@
+"""sampling::generate on the device (one CUDA graph per token) against a step-by-step
+replay: the same device logits (forward_rows), the oracle's CFG mix and the oracle's
+choose with its own MT19937 -- tokens must match exactly."""
+import numpy as np
+import pytest
+
+from oracle.oracle import OracleRng, cfg_mix
+from oracle.oracle import choose as ochoose
+from yue2_rs_b200 import Model, Phase, Request, Sampling, generate, generate_batch
+from yue2_rs_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def replay(model, prefix, negative, scale, s, seed, phase, legacy=False):
+    cond = model.new_cache(len(prefix) + s.max_tokens)
+    lc = model.forward_phase(prefix, cond, phase)
+    uncond = lu = None
+    if scale != 1.0:
+        uncond = model.new_cache(len(negative) + s.max_tokens)
+        lu = model.forward_phase(negative, uncond, phase)
+    rng = OracleRng(seed)
+    toks = []
+    for step in range(s.max_tokens):
+        mix = cfg_mix(lc, lu, scale) if uncond is not None else lc
+        t = ochoose(mix, s, toks, step, int(phase), legacy, rng)
+        if t == phase.end():
+            return toks, False
+        toks.append(t)
+        if step + 1 < s.max_tokens:
+            if uncond is not None:
+                lc, lu = model.forward_rows([cond, uncond], [t, t], phase)
+            else:
+                lc = model.forward_rows([cond], [t], phase)[0]
+    return toks, True
+
+
+@pytest.mark.parametrize("temperature", [1.0, 0.0])
+def test_generate_cfg_matches_replay(c1_device, c1_prompt, temperature):
+    prompt = c1_prompt[0][:40]
+    negative = c1_prompt[0][200:230]
+    s = Sampling(temperature, 0.93, 50, 1.2, 50, 0, 24)
+    g = generate(c1_device, prompt, s, 77, Phase.VOCAB, negative, 1.5)
+    want, trunc = replay(c1_device, prompt, negative, 1.5, s, 77, Phase.VOCAB)
+    assert g.tokens == want and g.truncated and trunc and len(g.tokens) == 24
+
+
+def test_generate_without_cfg_and_batch(c1_device, c1_prompt):
+    p = c1_prompt[0]
+    s = Sampling(1.0, 0.9, 40, 1.1, 20, 0, 12)
+    reqs = [Request(p[:17], 5), Request(p[30:50], 6, p[60:70], 1.5), Request(p[80:90], 7, p[90:99], 2.0, True)]
+    outs = generate_batch(c1_device, reqs, s, Phase.VOCAB)
+    for r, o in zip(reqs, outs):
+        want, _ = replay(c1_device, r.prefix, r.negative, r.scale, s, r.seed, Phase.VOCAB, r.legacy)
+        assert o.tokens == want
+
+
+def test_stop_token_ends_generation():
+    """A zero LM head makes every logit 0: greedy picks the lowest eligible id, which is
+    MUSIC_END (151852) as soon as step >= min_tokens, else CODEC_OFFSET."""
+    c = synth.config_c1()
+    c.vocab_size, c.num_hidden_layers = 184704, 1
+    m = Model(c)
+    from yue2_rs_b200 import _lib
+    _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, 3, 0.02))
+    m.set_tensor("lm_head.weight", np.zeros((c.vocab_size, c.hidden_size), dtype=np.uint16))
+    m.finalize()
+    s = Sampling(0.0, 0.95, 100, 1.2, 50, 5, 50)
+    g = generate(m, [1, 2, 3, 4], s, 1, Phase.SEMANTIC, [5, 6], 1.5)
+    assert g.tokens == [151853] * 5 and not g.truncated
+    m.close()

@@ -1,0 +1,107 @@
+// Host-side objects behind the opaque handles of include/yue2_cuda.h.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <map>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/yue2_cuda.h"
+#include "kernels.h"
+
+namespace y2 {
+
+// Fixed-size KV pages (kPageTokens positions of every layer) carved from cudaMalloc
+// chunks; a cache owns a page table of device addresses, so caches of any length
+// share one pool without fragmentation.
+struct PagePool {
+  size_t page_bytes = 0;
+  std::vector<void*> chunks;
+  std::vector<uint64_t> free_pages;
+  int take(size_t n, std::vector<uint64_t>& out);
+  void give(const std::vector<uint64_t>& pages);
+  void clear();
+};
+
+struct TensorSlot {
+  size_t offset = 0, rows = 0, cols = 0;
+  bool norm = false;  // f32 gain vector; matrices are bf16
+};
+
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+}  // namespace y2
+
+struct Yue2Model {
+  int device = 0;
+  Yue2Config cfg{};
+  y2::Geometry g{};
+  int sms = 148;
+  int gemv_grid = 148;
+  bool use_pdl = true, use_graphs = true;
+  bool finalized = false, workspace_ready = false;
+
+  char* arena = nullptr;
+  std::map<std::string, y2::TensorSlot> slots;
+  std::set<std::string> loaded;
+  uint16_t *embed = nullptr, *lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<y2::LayerW> layers;
+
+  float *cos_tab = nullptr, *sin_tab = nullptr;
+  int max_pos = 0;
+  y2::PagePool pool;
+
+  cudaStream_t stream = nullptr, side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+
+  // step workspace (kMaxRows rows)
+  float* x = nullptr;
+  uint16_t *qkv = nullptr, *qrot = nullptr, *attn = nullptr, *hbuf = nullptr;
+  float* logits = nullptr;
+  float* part = nullptr;
+  int32_t* counters = nullptr;
+  y2::DevRow* rows = nullptr;
+  int32_t* flags = nullptr;  // [0] token out of range, [1] position outside RoPE table
+  int max_splits = 64;
+  y2::DevRow* pinned_rows = nullptr;
+  int32_t* pinned_flags = nullptr;
+
+  std::map<int, cudaGraphExec_t> graphs;
+  std::vector<void*> allocations;
+
+  int alloc(void** p, size_t bytes);
+  int max_pos_limit() const {
+    return (int)(cfg.max_position_embeddings < (1u << 20) ? cfg.max_position_embeddings : (1u << 20));
+  }
+  ~Yue2Model();
+};
+
+struct Yue2Cache {
+  Yue2Model* m = nullptr;
+  std::vector<uint64_t> pages;
+  uint64_t* d_pages = nullptr;
+  uint64_t capacity = 0, length = 0;
+};
+
+struct Yue2Rng {
+  Yue2Model* m = nullptr;
+  y2::MtState* state = nullptr;
+};
+
+int y2_set_device(const Yue2Model* m);
+
+namespace y2 {
+int splits_for(const Yue2Model& m, int R);
+int check_phase_vocab(const Yue2Model& m, int phase);
+cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip);
+cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R, int dst_row, int phase,
+                        const int32_t* skip);
+int kernels_per_step(const Yue2Model& m, bool head, int phase);
+int run_forward(Yue2Model& m, int R, bool head, int phase);
+int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
+int take_flags(Yue2Model& m);
+int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
+}  // namespace y2

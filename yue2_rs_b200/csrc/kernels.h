@@ -1,0 +1,159 @@
+// Device-side structures and kernel launchers of the decode step.
+//
+// One decode "row" is one new token of one KV cache. A step processes R rows in a
+// single pass over every weight matrix (CFG cond + uncond rows, batched songs, or
+// consecutive prompt positions of one cache during prefill).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace y2 {
+
+// Token ids of the native protocol (src/protocol.rs:6-16 of the reference).
+constexpr int64_t kEOD = 151643;
+constexpr int64_t kAbcEnd = 151848;
+constexpr int64_t kMusicEnd = 151852;
+constexpr int64_t kCodecOffset = 151853;
+constexpr int64_t kCodecSize = 32768;
+constexpr int64_t kContext = 24576;
+
+enum Phase { kPhaseAbc = 0, kPhaseSemantic = 1, kPhaseVocab = 2 };
+
+constexpr int kMaxRows = 8;        // rows per weight pass on the CUDA-core GEMV
+constexpr int kPageTokens = 64;    // KV page: 64 positions of every layer
+constexpr int kPageLog2 = 6;
+
+struct DevRow {
+  const uint64_t* pages;  // device array: base address of each page of this row's cache
+  const int32_t* prompt;  // device ids of positions [prompt_begin, prompt_end)
+  int32_t pos;            // position of this row's token
+  int32_t token;          // token at `pos` outside the prompt range (sampler / host writes it)
+  int32_t prompt_begin, prompt_end;
+  int32_t active;         // 0: no KV write, no attention, no position advance
+  int32_t advance;        // positions added after each step
+};
+
+struct LayerW {
+  const uint16_t *q, *k, *v, *o, *gate, *up, *down;  // bf16 [out, in]
+  const float *in_norm, *q_norm, *k_norm, *post_norm;  // bf16-valued gains
+};
+
+struct Geometry {
+  int hidden, heads, kvh, dim, inter, vocab, layers;
+  float eps;
+};
+
+// Page layout: [layer][K=0 / V=1][kv head][kPageTokens][dim] bf16.
+__host__ __device__ inline size_t kv_offset(const Geometry& g, int layer, int kv, int head) {
+  return ((size_t)(layer * 2 + kv) * g.kvh + head) * kPageTokens * g.dim;
+}
+inline size_t page_bytes(const Geometry& g) { return (size_t)g.layers * 2 * g.kvh * kPageTokens * g.dim * 2; }
+
+// ---- GEMV (weight streaming, R <= kMaxRows rows per pass)
+enum XMode { kXBf16 = 0, kXNorm = 1, kXF32 = 2 };
+enum EpiMode { kEpiBf16 = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiLogits = 3, kEpiRawF32 = 4 };
+
+struct GemvParams {
+  const uint16_t* w[3];  // row segments; logical row n lives in segment s with seg_start[s] <= n
+  int seg_start[3];      // seg_start[0] = 0; unused segments start at N
+  int col0[3];           // output column of each segment's first row
+  const uint16_t* wpair;  // SwiGLU: up-projection rows paired with gate rows in w[0]
+  int N, K, R;
+  const uint16_t* xb;    // kXBf16: [R, K] bf16
+  const float* xf;       // kXNorm: residual [R, K]; kXF32: input [R, K]
+  const float* gamma;
+  float eps;
+  uint16_t* ob;          // bf16 outputs [R, ldo]
+  float* of;             // f32 outputs [R, ldo] (logits / raw) or residual [R, N]
+  int ldo;
+  const int32_t* skip;   // optional: the whole launch is skipped when *skip != 0
+};
+
+struct AttnParams {
+  const DevRow* rows;
+  const uint16_t* q;     // rotated queries [R, heads*dim] bf16
+  uint16_t* out;         // [R, heads*dim] bf16
+  float* part;           // split partials [R][kvh][S][G][dim + 2]
+  int32_t* counters;     // [R][kvh], zero between launches
+  Geometry g;
+  int layer, splits;
+  float scale;
+};
+
+struct RopeParams {
+  const DevRow* rows;
+  const uint16_t* qkv;   // [R, (heads + 2 kvh) * dim] bf16
+  uint16_t* q_out;       // [R, heads*dim]
+  const float* cos_tab;  // [max_pos, dim/2] bf16-valued
+  const float* sin_tab;
+  const float *q_norm, *k_norm;
+  Geometry g;
+  int layer, max_pos;
+  int32_t* error;        // set to 1 when a position is outside the RoPE table
+};
+
+// ---- sampler
+struct SampleCfg {  // protocol.rs Sampling
+  float temperature, top_p, repetition_penalty;
+  int32_t top_k, penalty_window, min_tokens, max_tokens;
+  int32_t phase;
+};
+
+struct SampleReq {
+  int32_t cond_row, uncond_row;  // logits rows; uncond_row < 0 without CFG
+  float scale;
+  int32_t legacy;
+  int32_t step;        // index of the sampling step (min_tokens gate)
+  int32_t hist_len;    // generated ids visible to the repetition penalty (tokens[0, hist_len))
+  int32_t done;
+  int32_t status;      // 0 or a negative YUE2_ERR_* code
+  int32_t truncated;   // 1 until the phase's stop id is drawn
+  int32_t last;        // id drawn by the latest step
+  int32_t bookkeeping; // 1: append to tokens, stop on the phase end id (generate); 0: draw only (choose)
+  int32_t pad;
+  int32_t* tokens;     // generated ids (device): history in, appended out
+};
+
+struct MtState {
+  uint32_t st[624];
+  uint32_t next;
+  uint32_t pad[3];
+};
+
+struct SampleParams {
+  const float* logits;
+  int ldl, vocab;
+  SampleCfg cfg;
+  SampleReq* reqs;
+  DevRow* rows;
+  const uint32_t* words;   // [nreq][2*vocab] MT words of this step
+  float* scores;           // scratch [nreq][vocab]
+  float* expv;             // scratch [nreq][vocab]
+  unsigned long long* sortbuf;  // scratch [nreq][sort_cap]
+  int sort_cap;            // power of two >= vocab
+  int32_t* live;           // requests not yet done; the last to finish sets *all_done
+  int32_t* all_done;
+};
+
+// launchers (return cudaError_t of the launch)
+cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const uint16_t* embed, int hidden,
+                         int vocab, float* x, int32_t* error);
+cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid);
+cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R);
+cudaError_t launch_attention(cudaStream_t s, bool pdl, const AttnParams& p, int R);
+cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R);
+cudaError_t launch_mt_words(cudaStream_t s, MtState* st, uint32_t* words, int nwords, const SampleReq* reqs,
+                            int nreq);
+cudaError_t launch_sample(cudaStream_t s, bool pdl, const SampleParams& p, int nreq);
+cudaError_t launch_fill_normal_bf16(cudaStream_t s, uint16_t* dst, size_t count, uint64_t seed, float mean,
+                                    float stddev);
+cudaError_t launch_fill_f32(cudaStream_t s, float* dst, size_t count, float value);
+cudaError_t launch_kv_fill(cudaStream_t s, const uint64_t* pages, const Geometry& g, int from, int to,
+                           uint64_t seed);
+
+cudaError_t prepare_kernels();  // configure every kernel for this device (call outside capture)
+size_t gemv_smem_bytes(int xmode, int K, int R);
+int attention_smem_bytes(int dim, int groups);
+
+}  // namespace y2

@@ -1,0 +1,738 @@
+// Per-layer decode kernels for sm_100a.
+//
+// Reference math (twally3/yue2_rs): Model::hidden decode branch (src/model.rs:523-591),
+// Norm::apply/heads (src/tensor.rs:1140-1172), Rotary (src/model.rs:137-168),
+// Linear::finish rounding (src/tensor.rs:1102-1118), Mlp::apply (src/model.rs:206-214),
+// decode attention (src/model.rs:314-397, src/attention.metal:206-317).
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace y2 {
+
+// ------------------------------------------------------------------ embed
+// x[r] = bf16(E[token_r]) (Model::embed, model.rs:452-464). The token of a row is the
+// prompt id of its position inside [prompt_begin, prompt_end), else row.token.
+__global__ void embed_kernel(DevRow* rows, int R, const uint16_t* __restrict__ embed, int hidden, int vocab,
+                             float* __restrict__ x, int32_t* error) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  if (r >= R) return;
+  DevRow& row = rows[r];
+  int tok = (row.pos >= row.prompt_begin && row.pos < row.prompt_end) ? row.prompt[row.pos - row.prompt_begin]
+                                                                      : row.token;
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) atomicExch(error, 1);
+    tok = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) row.token = tok;
+  const uint16_t* src = embed + (size_t)tok * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) x[(size_t)r * hidden + i] = bf2f(src[i]);
+}
+
+// When set, the launchers below only configure their kernel (no launch).
+static thread_local bool g_configure_only = false;
+
+// Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
+static cudaError_t ensure_smem_attr(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({fn, dev});
+  return e;
+}
+
+cudaError_t launch_with(cudaStream_t s, bool pdl, dim3 grid, dim3 block, size_t smem, const void* fn,
+                        void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const uint16_t* embed, int hidden,
+                         int vocab, float* x, int32_t* error) {
+  void* args[] = {&rows, &R, &embed, &hidden, &vocab, &x, &error};
+  return launch_with(s, pdl, dim3(R), dim3(256), 0, (const void*)embed_kernel, args);
+}
+
+// ------------------------------------------------------------------ GEMV
+// One warp streams one output row (or a gate/up row pair) at a time with 16-byte
+// L1-bypassing loads, double-buffered in registers across (row, batch) so the next
+// batch is in flight while the current one is reduced. Activations sit in shared
+// memory (bf16, or f32 for raw drop-in inputs). The first batch of weights is
+// requested before griddepcontrol.wait, overlapping the previous kernel's tail.
+template <int XM>
+struct XTraits;
+template <>
+struct XTraits<kXBf16> {
+  static constexpr int bytes = 2;
+};
+template <>
+struct XTraits<kXNorm> {
+  static constexpr int bytes = 2;
+};
+template <>
+struct XTraits<kXF32> {
+  static constexpr int bytes = 4;
+};
+
+Y2_DEV float dot8_f32(uint4 w, const float4& a, const float4& b, float acc) {
+  acc = fmaf(bf_lo(w.x), a.x, acc);
+  acc = fmaf(bf_hi(w.x), a.y, acc);
+  acc = fmaf(bf_lo(w.y), a.z, acc);
+  acc = fmaf(bf_hi(w.y), a.w, acc);
+  acc = fmaf(bf_lo(w.z), b.x, acc);
+  acc = fmaf(bf_hi(w.z), b.y, acc);
+  acc = fmaf(bf_lo(w.w), b.z, acc);
+  acc = fmaf(bf_hi(w.w), b.w, acc);
+  return acc;
+}
+
+// Block-wide f32 sum with a fixed reduction order (identical in every CTA).
+Y2_DEV float block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+template <int RM, bool PAIR, int XM, int EPI, int CH>
+__global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[32];
+  constexpr int NP = PAIR ? 2 : 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int K = p.K, K8 = K >> 3;
+  const int nb = (K8 + 32 * CH - 1) / (32 * CH);
+  const int row_begin = (int)(((long long)p.N * blockIdx.x) / gridDim.x);
+  const int row_end = (int)(((long long)p.N * (blockIdx.x + 1)) / gridDim.x);
+  const int first = row_begin + warp;
+  const int nrows_w = first < row_end ? (row_end - first + nwarps - 1) / nwarps : 0;
+  const int T = nrows_w * nb;
+
+  auto wrow = [&](int n) -> const uint16_t* {
+    const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
+    return p.w[s] + (size_t)(n - p.seg_start[s]) * K;
+  };
+  auto load = [&](uint4(&buf)[NP][CH], int t) {
+    const int n = first + (t / nb) * nwarps, b = t % nb;
+    const uint16_t* w0 = wrow(n);
+    const uint16_t* w1 = PAIR ? p.wpair + (size_t)n * K : nullptr;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = (b * CH + c) * 32 + lane;
+      if (idx < K8) {
+        buf[0][c] = ldg_stream(w0 + (size_t)idx * 8);
+        if (PAIR) buf[NP - 1][c] = ldg_stream(w1 + (size_t)idx * 8);
+      } else {
+        buf[0][c] = make_uint4(0, 0, 0, 0);
+        if (PAIR) buf[NP - 1][c] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  uint4 A[NP][CH], B[NP][CH];
+  if (T > 0) load(A, 0);
+
+  pdl_wait();
+  pdl_trigger();
+  if (p.skip && *p.skip) return;
+
+  // ---- stage activations
+  if (XM == kXF32) {
+    float* xs = reinterpret_cast<float*>(smem_raw);
+    for (int i = threadIdx.x; i < RM * K; i += blockDim.x) {
+      const int r = i / K;
+      xs[i] = r < p.R ? p.xf[i] : 0.f;
+    }
+  } else if (XM == kXBf16) {
+    uint4* xs = reinterpret_cast<uint4*>(smem_raw);
+    for (int i = threadIdx.x; i < RM * K8; i += blockDim.x) {
+      const int r = i / K8;
+      xs[i] = r < p.R ? ldg16(p.xb + (size_t)i * 8) : make_uint4(0, 0, 0, 0);
+    }
+  } else {  // kXNorm: RMSNorm of the f32 residual, bf16 rounded as Norm::apply does
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);
+    for (int r = 0; r < RM; ++r) {
+      if (r >= p.R) {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[r * K + i] = 0;
+        continue;
+      }
+      const float* xr = p.xf + (size_t)r * K;
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+      ss = block_sum(ss, red);
+      const float scale = round_bf16(1.0f / sqrtf(ss / (float)K + p.eps));
+      for (int i = threadIdx.x; i < K; i += blockDim.x)
+        xs[r * K + i] = f2bf_exact(round_bf16(round_bf16(xr[i] * scale) * p.gamma[i]));
+    }
+  }
+  __syncthreads();
+
+  float acc[NP][RM];
+#pragma unroll
+  for (int q = 0; q < NP; ++q)
+#pragma unroll
+    for (int r = 0; r < RM; ++r) acc[q][r] = 0.f;
+
+  auto finish = [&](int n) {
+#pragma unroll
+    for (int q = 0; q < NP; ++q)
+#pragma unroll
+      for (int r = 0; r < RM; ++r) acc[q][r] = warp_sum(acc[q][r]);
+    if (lane == 0) {
+      const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
+      const int col = p.col0[s] + (n - p.seg_start[s]);
+#pragma unroll
+      for (int r = 0; r < RM; ++r) {
+        if (r >= p.R) break;
+        if (EPI == kEpiBf16) {
+          p.ob[(size_t)r * p.ldo + col] = f2bf_round(acc[0][r]);
+        } else if (EPI == kEpiResidual) {
+          float* xr = p.of + (size_t)r * p.ldo + col;
+          *xr = round_bf16(*xr + round_bf16(acc[0][r]));
+        } else if (EPI == kEpiSwiGLU) {
+          const float g = round_bf16(acc[0][r]);
+          const float u = round_bf16(acc[NP - 1][r]);
+          const float a = round_bf16(g / (1.0f + det_expf(-g)));
+          p.ob[(size_t)r * p.ldo + col] = f2bf_round(a * u);
+        } else if (EPI == kEpiLogits) {
+          p.of[(size_t)r * p.ldo + col] = round_bf16(acc[0][r]);
+        } else {
+          p.of[(size_t)r * p.ldo + col] = acc[0][r];
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < NP; ++q)
+#pragma unroll
+      for (int r = 0; r < RM; ++r) acc[q][r] = 0.f;
+  };
+
+  auto compute = [&](const uint4(&buf)[NP][CH], int t) {
+    const int b = t % nb;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = (b * CH + c) * 32 + lane;
+      if (idx < K8) {
+#pragma unroll
+        for (int r = 0; r < RM; ++r) {
+          if (XM == kXF32) {
+            const float4* xs = reinterpret_cast<const float4*>(smem_raw) + ((size_t)r * K8 + idx) * 2;
+            const float4 a = xs[0], bb = xs[1];
+#pragma unroll
+            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_f32(buf[q][c], a, bb, acc[q][r]);
+          } else {
+            const uint4 xv = reinterpret_cast<const uint4*>(smem_raw)[(size_t)r * K8 + idx];
+#pragma unroll
+            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_bf(buf[q][c], xv, acc[q][r]);
+          }
+        }
+      }
+    }
+    if (b == nb - 1) finish(first + (t / nb) * nwarps);
+  };
+
+  for (int t = 0; t < T; t += 2) {
+    if (t + 1 < T) load(B, t + 1);
+    compute(A, t);
+    if (t + 1 >= T) break;
+    if (t + 2 < T) load(A, t + 2);
+    compute(B, t + 1);
+  }
+}
+
+size_t gemv_smem_bytes(int xmode, int K, int R) {
+  const int rm = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
+  return (size_t)rm * K * (xmode == kXF32 ? 4 : 2);
+}
+
+template <int RM, bool PAIR, int XM, int EPI, int CH>
+static cudaError_t gemv_go(cudaStream_t s, bool pdl, const GemvParams& p, int grid) {
+  const void* fn = (const void*)gemv_kernel<RM, PAIR, XM, EPI, CH>;
+  const size_t smem = (size_t)RM * p.K * XTraits<XM>::bytes;
+  cudaError_t e = ensure_smem_attr(fn, 200 * 1024);
+  if (e != cudaSuccess || g_configure_only) return e;
+  GemvParams copy = p;
+  void* args[] = {&copy};
+  return launch_with(s, pdl, dim3(grid), dim3(256), smem, fn, args);
+}
+
+template <bool PAIR, int XM, int EPI, int CH>
+static cudaError_t gemv_rows(cudaStream_t s, bool pdl, const GemvParams& p, int grid) {
+  if (p.R <= 1) return gemv_go<1, PAIR, XM, EPI, CH>(s, pdl, p, grid);
+  if (p.R <= 2) return gemv_go<2, PAIR, XM, EPI, CH>(s, pdl, p, grid);
+  if (p.R <= 4) return gemv_go<4, PAIR, XM, EPI, CH>(s, pdl, p, grid);
+  return gemv_go<8, PAIR, XM, EPI, CH>(s, pdl, p, grid);
+}
+
+cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
+  if (p.R < 1 || p.R > kMaxRows || (p.K & 7) || p.N < 1) return cudaErrorInvalidValue;
+  const int K8 = p.K >> 3;
+  // chunks per lane per batch: whole batches where the row length allows it
+  const bool c8 = (K8 % 256) == 0, c6 = (K8 % 192) == 0;
+  switch (epi) {
+    case kEpiBf16:
+      if (xmode == kXNorm) return c8 ? gemv_rows<false, kXNorm, kEpiBf16, 8>(s, pdl, p, grid)
+                                : c6 ? gemv_rows<false, kXNorm, kEpiBf16, 6>(s, pdl, p, grid)
+                                     : gemv_rows<false, kXNorm, kEpiBf16, 4>(s, pdl, p, grid);
+      break;
+    case kEpiResidual:
+      if (xmode == kXBf16) return c8 ? gemv_rows<false, kXBf16, kEpiResidual, 8>(s, pdl, p, grid)
+                                : c6 ? gemv_rows<false, kXBf16, kEpiResidual, 6>(s, pdl, p, grid)
+                                     : gemv_rows<false, kXBf16, kEpiResidual, 4>(s, pdl, p, grid);
+      break;
+    case kEpiSwiGLU:
+      if (xmode == kXNorm) return gemv_rows<true, kXNorm, kEpiSwiGLU, 4>(s, pdl, p, grid);
+      break;
+    case kEpiLogits:
+      if (xmode == kXNorm) return c8 ? gemv_rows<false, kXNorm, kEpiLogits, 8>(s, pdl, p, grid)
+                                : c6 ? gemv_rows<false, kXNorm, kEpiLogits, 6>(s, pdl, p, grid)
+                                     : gemv_rows<false, kXNorm, kEpiLogits, 4>(s, pdl, p, grid);
+      if (xmode == kXBf16) return gemv_rows<false, kXBf16, kEpiLogits, 4>(s, pdl, p, grid);
+      break;
+    case kEpiRawF32:
+      if (xmode == kXF32 && p.R == 1) return gemv_go<1, false, kXF32, kEpiRawF32, 4>(s, pdl, p, grid);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ QK norm + RoPE + KV append
+// One warp per (head, row): q heads are normalised (Norm::heads) and rotated, k heads
+// normalised, rotated and written to the row's page at its position, v heads copied.
+template <int D>
+__global__ void __launch_bounds__(32) rope_append_kernel(const RopeParams p) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int DL = D / 32, HALF = D / 2;
+  __shared__ float v[D];
+  const int hix = blockIdx.x, r = blockIdx.y, lane = threadIdx.x;
+  const DevRow row = p.rows[r];
+  if (!row.active) return;
+  const Geometry& g = p.g;
+  const int pos = row.pos;
+  if (pos < 0 || pos >= p.max_pos) {
+    if (lane == 0) atomicExch(p.error, 1);
+    return;
+  }
+  const int width = (g.heads + 2 * g.kvh) * D;
+  const uint16_t* src = p.qkv + (size_t)r * width + (size_t)hix * D;
+  uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
+  const int slot = pos & (kPageTokens - 1);
+  if (hix >= g.heads + g.kvh) {  // value head: already bf16 (Linear::finish)
+    const int head = hix - g.heads - g.kvh;
+    uint16_t* dst = page + kv_offset(g, p.layer, 1, head) + (size_t)slot * D;
+    for (int i = lane; i < D; i += 32) dst[i] = src[i];
+    return;
+  }
+  const bool is_q = hix < g.heads;
+  const float* gamma = is_q ? p.q_norm : p.k_norm;
+  float x[DL];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < DL; ++e) {
+    x[e] = bf2f(src[lane * DL + e]);
+    ss = fmaf(x[e], x[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float scale = round_bf16(1.0f / sqrtf(ss / (float)D + g.eps));
+#pragma unroll
+  for (int e = 0; e < DL; ++e) v[lane * DL + e] = round_bf16(round_bf16(x[e] * scale) * gamma[lane * DL + e]);
+  __syncwarp();
+  const float* ct = p.cos_tab + (size_t)pos * HALF;
+  const float* st = p.sin_tab + (size_t)pos * HALF;
+  uint16_t* dst = is_q ? p.q_out + (size_t)r * g.heads * D + (size_t)hix * D
+                       : page + kv_offset(g, p.layer, 0, hix - g.heads) + (size_t)slot * D;
+  for (int i = lane; i < HALF; i += 32) {
+    const float a = v[i], b = v[i + HALF], c = ct[i], s = st[i];
+    dst[i] = f2bf_round(round_bf16(a * c) - round_bf16(b * s));
+    dst[i + HALF] = f2bf_round(round_bf16(b * c) + round_bf16(a * s));
+  }
+}
+
+cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R) {
+  RopeParams copy = p;
+  void* args[] = {&copy};
+  dim3 grid(p.g.heads + 2 * p.g.kvh, R);
+  switch (p.g.dim) {
+    case 64: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<64>, args);
+    case 128: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<128>, args);
+    case 256: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<256>, args);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ decode attention
+// Split-K flash decoding. CTA (split, kv head, row) owns a contiguous range of 32-key
+// tiles of the row's cache; each warp stages a tile of K (XOR-swizzled, conflict-free
+// for lane-per-key reads) and V into shared memory with cp.async, computes the G
+// grouped heads' scores with one key per lane, updates an online softmax, and
+// accumulates P.V with lanes over head dims. Warps merge in shared memory; splits
+// merge through f32 partials, and the last split CTA to finish (atomic ticket; no
+// waiting) normalises and writes the bf16 output.
+template <int D, int G>
+__global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int CPR = D / 8;  // 16-byte chunks per key row
+  constexpr int DL = D / 32;  // dims per lane
+  constexpr int NW = 4;
+  uint16_t* ktile = reinterpret_cast<uint16_t*>(smem_raw);           // [NW][32][D]
+  uint16_t* vtile = ktile + NW * 32 * D;                               // [NW][32][D]
+  float* qs = reinterpret_cast<float*>(vtile + NW * 32 * D);           // [G][D]
+  float* ps = qs + G * D;                                              // [NW][G][32]
+  float* wm = ps + NW * G * 32;                                        // [NW][G]
+  float* wl = wm + NW * G;                                             // [NW][G]
+  __shared__ int s_ticket;
+
+  pdl_wait();
+  pdl_trigger();
+  const int split = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DevRow row = a.rows[r];
+  if (!row.active) return;
+  const Geometry& geo = a.g;
+  const int keys = row.pos + 1;
+  const int ntiles = (keys + 31) >> 5;
+  const int tps = (ntiles + a.splits - 1) / a.splits;
+  const int nsplit = (ntiles + tps - 1) / tps;
+  if (split >= nsplit) return;
+  const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
+
+  const uint16_t* qsrc = a.q + (size_t)r * geo.heads * D + (size_t)g * G * D;
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = bf2f(qsrc[i]);
+  __syncthreads();
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
+  }
+  uint16_t* kt = ktile + warp * 32 * D;
+  uint16_t* vt = vtile + warp * 32 * D;
+  float* pw = ps + warp * G * 32;
+  const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
+
+  for (int t = t0 + warp; t < t1; t += NW) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
+    const uint16_t* kb = page + koff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int j = i / CPR, c = i % CPR;
+      if (j < nk) {
+        cp_async16(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
+        cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.f;
+    if (lane < nk) {
+#pragma unroll 4
+      for (int c = 0; c < CPR; ++c) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(kt + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
+        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+        const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + c * 8 + 4);
+          float s = sc[h];
+          s = fmaf(qa.x, k0, s);
+          s = fmaf(qa.y, k1, s);
+          s = fmaf(qa.z, k2, s);
+          s = fmaf(qa.w, k3, s);
+          s = fmaf(qb.x, k4, s);
+          s = fmaf(qb.y, k5, s);
+          s = fmaf(qb.z, k6, s);
+          s = fmaf(qb.w, k7, s);
+          sc[h] = s;
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
+      const float mnew = fmaxf(m[h], warp_max(s));
+      const float alpha = m[h] == -INFINITY ? 0.f : __expf(m[h] - mnew);
+      const float pv = lane < nk ? __expf(s - mnew) : 0.f;
+      l[h] = l[h] * alpha + warp_sum(pv);
+      m[h] = mnew;
+      pw[h * 32 + lane] = pv;
+#pragma unroll
+      for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
+    }
+    __syncwarp();
+    for (int j = 0; j < nk; ++j) {
+      const uint16_t* vr = vt + (size_t)j * D + lane * DL;
+      float vv[DL];
+      if constexpr (DL == 2) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
+        vv[0] = bf_lo(w);
+        vv[1] = bf_hi(w);
+      } else if constexpr (DL == 4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(vr);
+        vv[0] = bf_lo(w.x);
+        vv[1] = bf_hi(w.x);
+        vv[2] = bf_lo(w.y);
+        vv[3] = bf_hi(w.y);
+      } else {
+        const uint4 w = *reinterpret_cast<const uint4*>(vr);
+        vv[0] = bf_lo(w.x);
+        vv[1] = bf_hi(w.x);
+        vv[2] = bf_lo(w.y);
+        vv[3] = bf_hi(w.y);
+        vv[4] = bf_lo(w.z);
+        vv[5] = bf_hi(w.z);
+        vv[6] = bf_lo(w.w);
+        vv[7] = bf_hi(w.w);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float pj = pw[h * 32 + j];
+#pragma unroll
+        for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
+  __syncthreads();
+  float* wacc = reinterpret_cast<float*>(smem_raw);
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      wm[warp * G + h] = m[h];
+      wl[warp * G + h] = l[h];
+    }
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int e = 0; e < DL; ++e) wacc[((size_t)warp * G + h) * D + lane * DL + e] = acc[h][e];
+  __syncthreads();
+
+  const int outw = geo.heads * D;
+  float* part = a.part + ((size_t)(r * geo.kvh + g) * a.splits) * G * (D + 2);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * G + h]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float mw = wm[w * G + h];
+      if (mw == -INFINITY) continue;
+      const float f = __expf(mw - M);
+      L = fmaf(wl[w * G + h], f, L);
+      O = fmaf(wacc[((size_t)w * G + h) * D + d], f, O);
+    }
+    if (nsplit == 1) {
+      a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
+    } else {
+      float* ph = part + ((size_t)split * G + h) * (D + 2);
+      if (d == 0) {
+        ph[0] = M;
+        ph[1] = L;
+      }
+      ph[2 + d] = O;
+    }
+  }
+  if (nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(a.counters + r * geo.kvh + g, 1);
+  __syncthreads();
+  if (s_ticket != nsplit - 1) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(part + ((size_t)s * G + h) * (D + 2)));
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float* ph = part + ((size_t)s * G + h) * (D + 2);
+      const float f = __expf(__ldcg(ph) - M);
+      L = fmaf(__ldcg(ph + 1), f, L);
+      O = fmaf(__ldcg(ph + 2 + d), f, O);
+    }
+    a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
+  }
+  if (threadIdx.x == 0) a.counters[r * geo.kvh + g] = 0;
+}
+
+int attention_smem_bytes(int dim, int groups) {
+  const int tiles = 2 * 4 * 32 * dim * 2;
+  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups) * 4;
+  const int merge = 4 * groups * dim * 4;
+  return (tiles > merge ? tiles : merge) + extra;
+}
+
+template <int D, int G>
+static cudaError_t attn_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
+  const void* fn = (const void*)attn_kernel<D, G>;
+  const int smem = attention_smem_bytes(D, G);
+  cudaError_t e = ensure_smem_attr(fn, smem);
+  if (e != cudaSuccess || g_configure_only) return e;
+  AttnParams copy = p;
+  void* args[] = {&copy};
+  return launch_with(s, pdl, dim3(p.splits, p.g.kvh, R), dim3(128), smem, fn, args);
+}
+
+template <int D>
+static cudaError_t attn_dim(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
+  switch (p.g.heads / p.g.kvh) {
+    case 1: return attn_go<D, 1>(s, pdl, p, R);
+    case 2: return attn_go<D, 2>(s, pdl, p, R);
+    case 3: return attn_go<D, 3>(s, pdl, p, R);
+    case 4: return attn_go<D, 4>(s, pdl, p, R);
+    case 8: return attn_go<D, 8>(s, pdl, p, R);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_attention(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
+  switch (p.g.dim) {
+    case 64: return attn_dim<64>(s, pdl, p, R);
+    case 128: return attn_dim<128>(s, pdl, p, R);
+    case 256: return attn_dim<256>(s, pdl, p, R);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Sets the shared-memory attribute of every GEMV and attention instantiation on the
+// current device, so that no attribute call happens while a CUDA graph is captured.
+cudaError_t prepare_kernels() {
+  g_configure_only = true;
+  cudaError_t e = cudaSuccess;
+  const int pairs[][2] = {{kXNorm, kEpiBf16}, {kXBf16, kEpiResidual}, {kXNorm, kEpiSwiGLU},
+                          {kXNorm, kEpiLogits}, {kXBf16, kEpiLogits}, {kXF32, kEpiRawF32}};
+  for (auto& pr : pairs)
+    for (int K : {2048, 1536, 1024})
+      for (int R : {1, 2, 4, 8}) {
+        GemvParams p = {};
+        p.K = K;
+        p.N = 1;
+        p.R = pr[0] == kXF32 ? 1 : R;
+        if (e == cudaSuccess) e = launch_gemv(nullptr, false, pr[0], pr[1], p, 1);
+      }
+  for (int D : {64, 128, 256})
+    for (int G : {1, 2, 3, 4, 8}) {
+      AttnParams a = {};
+      a.g.dim = D;
+      a.g.kvh = 1;
+      a.g.heads = G;
+      if (e == cudaSuccess) e = launch_attention(nullptr, false, a, 1);
+    }
+  g_configure_only = false;
+  return e;
+}
+
+// ------------------------------------------------------------------ step bookkeeping
+__global__ void step_end_kernel(DevRow* rows, int R) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = threadIdx.x;
+  if (r < R && rows[r].active) rows[r].pos += rows[r].advance;
+}
+
+cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R) {
+  void* args[] = {&rows, &R};
+  return launch_with(s, pdl, dim3(1), dim3(32), 0, (const void*)step_end_kernel, args);
+}
+
+// ------------------------------------------------------------------ synthetic data
+Y2_DEV uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+Y2_DEV float normal_at(uint64_t seed, uint64_t i) {
+  const uint64_t z = mix64(seed + (i >> 1) * 0x9E3779B97F4A7C15ull);
+  const float u1 = ((uint32_t)(z >> 40) + 1) * (1.0f / 16777217.0f);
+  const float u2 = (uint32_t)(z & 0xffffff) * (1.0f / 16777216.0f);
+  const float rad = sqrtf(-2.0f * logf(u1));
+  return (i & 1) ? rad * sinf(6.2831853071795865f * u2) : rad * cosf(6.2831853071795865f * u2);
+}
+
+__global__ void fill_normal_kernel(uint16_t* dst, size_t count, uint64_t seed, float mean, float stddev) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = f2bf_round(mean + stddev * normal_at(seed, i));
+}
+
+cudaError_t launch_fill_normal_bf16(cudaStream_t s, uint16_t* dst, size_t count, uint64_t seed, float mean,
+                                    float stddev) {
+  fill_normal_kernel<<<1184, 256, 0, s>>>(dst, count, seed, mean, stddev);
+  return cudaGetLastError();
+}
+
+__global__ void fill_f32_kernel(float* dst, size_t count, float value) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = value;
+}
+
+cudaError_t launch_fill_f32(cudaStream_t s, float* dst, size_t count, float value) {
+  fill_f32_kernel<<<592, 256, 0, s>>>(dst, count, value);
+  return cudaGetLastError();
+}
+
+// Seeded N(0,1) bf16 keys/values for positions [from, to) of every layer.
+__global__ void kv_fill_kernel(const uint64_t* pages, Geometry g, int from, int to, uint64_t seed) {
+  const size_t per_tok = (size_t)g.layers * 2 * g.kvh * g.dim;
+  const size_t total = per_tok * (size_t)(to - from);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int tok = from + (int)(i / per_tok);
+    size_t rem = i % per_tok;
+    const int d = (int)(rem % g.dim);
+    rem /= g.dim;
+    const int head = (int)(rem % g.kvh);
+    rem /= g.kvh;
+    const int kv = (int)(rem % 2);
+    const int layer = (int)(rem / 2);
+    uint16_t* page = reinterpret_cast<uint16_t*>(pages[tok >> kPageLog2]);
+    const uint64_t flat = (((uint64_t)layer * 2 + kv) * g.kvh + head) * 1048576ull * 64 + (uint64_t)tok * g.dim + d;
+    page[kv_offset(g, layer, kv, head) + (size_t)(tok & (kPageTokens - 1)) * g.dim + d] =
+        f2bf_round(normal_at(seed, flat));
+  }
+}
+
+cudaError_t launch_kv_fill(cudaStream_t s, const uint64_t* pages, const Geometry& g, int from, int to,
+                           uint64_t seed) {
+  if (to <= from) return cudaSuccess;
+  kv_fill_kernel<<<1184, 256, 0, s>>>(pages, g, from, to, seed);
+  return cudaGetLastError();
+}
+
+}  // namespace y2

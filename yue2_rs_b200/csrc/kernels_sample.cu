@@ -1,0 +1,405 @@
+// On-device CFG mix, sampler and MT19937 stream for sm_100a.
+//
+// Reference: sampling::generate CFG mix (src/sampling.rs:261-266), sampling::choose
+// (src/sampling.rs:103-215), Generator (src/sampling.rs:10-62). Token ids are bit-exact
+// with the reference algorithm given identical logits: every float operation of
+// `choose` is reproduced in the same order where the order matters (the sequential
+// top-p and normalisation sums run on one lane), and exp/ln_1p come from detmath.h.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace y2 {
+
+// ------------------------------------------------------------------ MT19937
+// Twist in four dependency phases: [0,227) reads only old words, [227,454) reads
+// words from the first phase, [454,623) from the second, and 623 reads the new
+// words 0 and 396. Each phase reads everything before any thread writes.
+Y2_DEV void mt_phase(uint32_t* st, int lo, int hi) {
+  const int i = lo + (int)threadIdx.x;
+  const bool act = i < hi;
+  uint32_t v = 0;
+  if (act) {
+    const uint32_t y = (st[i] & 0x80000000u) | (st[(i + 1) % 624] & 0x7fffffffu);
+    v = st[(i + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+  }
+  __syncthreads();
+  if (act) st[i] = v;
+  __syncthreads();
+}
+
+Y2_DEV uint32_t mt_temper(uint32_t y) {
+  y ^= y >> 11;
+  y ^= (y << 7) & 0x9d2c5680u;
+  y ^= (y << 15) & 0xefc60000u;
+  y ^= y >> 18;
+  return y;
+}
+
+// Emits the next `nwords` tempered outputs of each request's generator (one CTA per
+// request) and advances its state; the stream depends only on the seed and on how
+// many words were consumed, so it runs beside the forward pass.
+__global__ void __launch_bounds__(256) mt_words_kernel(MtState* states, uint32_t* words, int nwords,
+                                                        const SampleReq* reqs) {
+  const int b = blockIdx.x;
+  if (reqs && reqs[b].done) return;
+  __shared__ uint32_t st[624];
+  MtState* S = states + b;
+  for (int i = threadIdx.x; i < 624; i += blockDim.x) st[i] = S->st[i];
+  uint32_t next = S->next;
+  __syncthreads();
+  uint32_t* out = words + (size_t)b * nwords;
+  int pos = 0;
+  while (pos < nwords) {
+    if (next == 624) {
+      mt_phase(st, 0, 227);
+      mt_phase(st, 227, 454);
+      mt_phase(st, 454, 623);
+      mt_phase(st, 623, 624);
+      next = 0;
+    }
+    const int n = min(624 - (int)next, nwords - pos);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[pos + i] = mt_temper(st[next + i]);
+    pos += n;
+    next += n;
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < 624; i += blockDim.x) S->st[i] = st[i];
+  if (threadIdx.x == 0) S->next = next;
+}
+
+cudaError_t launch_mt_words(cudaStream_t s, MtState* st, uint32_t* words, int nwords, const SampleReq* reqs,
+                            int nreq) {
+  mt_words_kernel<<<nreq, 256, 0, s>>>(st, words, nwords, reqs);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ sampler
+Y2_DEV float cast(float x, bool legacy) { return legacy ? round_bf16(x) : x; }
+
+// ascending order of this key == score descending (total order), id ascending
+Y2_DEV unsigned long long composite(float s, int id) {
+  return ((unsigned long long)(~total_key(s)) << 32) | (uint32_t)id;
+}
+
+template <typename T>
+Y2_DEV void bitonic_sort(T* a, int m) {
+  for (int k = 2; k <= m; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const T x = a[i], y = a[ixj];
+          const bool up = (i & k) == 0;
+          if ((x > y) == up) {
+            a[i] = y;
+            a[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
+
+constexpr int kSmemSort = 2048;
+constexpr int kSampleThreads = 1024;
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
+  __shared__ unsigned long long srt_s[kSmemSort];
+  __shared__ uint32_t hist[256];
+  __shared__ int s_count, s_nkeep;
+  __shared__ uint32_t s_prefix, s_target;
+  __shared__ unsigned long long s_best[32];
+  __shared__ float s_sum;
+
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
+  SampleReq& q = p.reqs[b];
+  if (q.done) return;
+  const int V = p.vocab;
+  const SampleCfg c = p.cfg;
+  const bool legacy = q.legacy != 0;
+  float* S = p.scores + (size_t)b * V;
+  const float* lc = p.logits + (size_t)q.cond_row * p.ldl;
+  const float* lu = q.uncond_row >= 0 ? p.logits + (size_t)q.uncond_row * p.ldl : nullptr;
+  const int step = q.step, hlen = q.hist_len;
+
+  auto finish = [&](int status, int id) {  // thread 0 only
+    q.last = id;
+    q.status = status;
+    bool newly_done = false;
+    if (status != 0) {
+      newly_done = true;
+    } else if (q.bookkeeping) {
+      const int stop = c.phase == kPhaseAbc ? (int)kAbcEnd : c.phase == kPhaseSemantic ? (int)kMusicEnd : -1;
+      if (id == stop) {
+        q.truncated = 0;
+        newly_done = true;
+      } else {
+        q.tokens[step] = id;
+        q.step = step + 1;
+        q.hist_len = hlen + 1;
+        p.rows[q.cond_row].token = id;
+        if (q.uncond_row >= 0) p.rows[q.uncond_row].token = id;
+        if (step + 1 >= c.max_tokens) newly_done = true;
+      }
+    }
+    if (newly_done && q.bookkeeping) {
+      q.done = 1;
+      p.rows[q.cond_row].active = 0;
+      if (q.uncond_row >= 0) p.rows[q.uncond_row].active = 0;
+      if (p.live && atomicSub(p.live, 1) == 1) *p.all_done = 1;
+    }
+  };
+
+  // ---- A: CFG mix (sampling.rs:261-266) and phase window (sampling.rs:112-129)
+  int w0 = 0, w1 = V, stop = -1;
+  if (c.phase == kPhaseAbc) {
+    w1 = (int)kEOD;
+    stop = (int)kAbcEnd;
+  } else if (c.phase == kPhaseSemantic) {
+    w0 = (int)kCodecOffset;
+    w1 = (int)(kCodecOffset + kCodecSize);
+    stop = (int)kMusicEnd;
+  }
+  const bool stop_on = stop >= 0 && step >= c.min_tokens;
+  for (int i = tid; i < V; i += nt) {
+    float l = lc[i];
+    if (lu) {
+      const float u = lu[i];
+      l = round_bf16(u + round_bf16(q.scale * round_bf16(l - u)));
+    }
+    const bool in = (i >= w0 && i < w1) || (stop_on && i == stop);
+    S[i] = in ? l : -INFINITY;
+  }
+  __syncthreads();
+
+  // ---- B: repetition penalty over the last penalty_window ids (sampling.rs:130-144)
+  {
+    const int from = max(0, hlen - c.penalty_window);
+    const int n = hlen - from;
+    if (tid < n) {
+      const int id = q.tokens[from + tid];
+      bool first = true;
+      int cnt = 0;
+      for (int j = 0; j < n; ++j)
+        if (q.tokens[from + j] == id) {
+          if (j < tid) first = false;
+          ++cnt;
+        }
+      if (first && id >= 0 && id < V) {
+        const float alpha = cast(powi_f32(c.repetition_penalty, cnt), legacy);
+        const float s = S[id];
+        S[id] = cast(s < 0.f ? s * alpha : s / alpha, legacy);
+      }
+    }
+  }
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+
+  // ---- C: invalid logits, temperature, finite count (sampling.rs:145-167)
+  const bool t0 = c.temperature == 0.f, t1 = c.temperature == 1.f;
+  int bad = 0, nfin = 0;
+  unsigned long long best = ~0ull;
+  for (int i = tid; i < V; i += nt) {
+    float s = S[i];
+    if (isnan(s) || s == INFINITY) bad = 1;
+    if (t0) {
+      if (isfinite(s)) best = min(best, composite(s, i));
+      continue;
+    }
+    if (!t1) {
+      s = cast(s / c.temperature, legacy);
+      S[i] = s;
+    }
+    nfin += isfinite(s) ? 1 : 0;
+  }
+  if (__syncthreads_or(bad)) {
+    if (tid == 0) finish(-5, -1);
+    return;
+  }
+  if (t0) {  // greedy: highest total-order score, lowest id (sampling.rs:148-156)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (lane == 0) s_best[warp] = best;
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long bb = ~0ull;
+      for (int w = 0; w < nt / 32; ++w) bb = min(bb, s_best[w]);
+      if (bb == ~0ull) finish(-6, -1);
+      else finish(0, (int)(bb & 0xffffffffu));
+    }
+    return;
+  }
+  atomicAdd(&s_count, nfin);
+  __syncthreads();
+  const int n_finite = s_count;
+  if (n_finite == 0) {
+    if (tid == 0) finish(-6, -1);
+    return;
+  }
+
+  // ---- D: exact threshold = score at descending rank min(top_k-1, n-1) (select_nth, :168-172)
+  const int rank = (int)min((long long)c.top_k - 1, (long long)n_finite - 1);
+  uint32_t prefix = 0, mask = 0;
+  uint32_t target = (uint32_t)rank;
+  const int iters = (V + nt - 1) / nt;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += nt) hist[i] = 0;
+    __syncthreads();
+    for (int it = 0; it < iters; ++it) {
+      const int i = it * nt + tid;
+      uint32_t d = 256;
+      if (i < V) {
+        const float s = S[i];
+        if (isfinite(s)) {
+          const uint32_t k = total_key(s);
+          if ((k & mask) == prefix) d = (k >> shift) & 255u;
+        }
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, d);
+      if (d < 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[d], (uint32_t)__popc(peers));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t cum = 0;
+      for (int d = 255; d >= 0; --d) {
+        if (cum + hist[d] > target) {
+          s_prefix = prefix | ((uint32_t)d << shift);
+          s_target = target - cum;
+          break;
+        }
+        cum += hist[d];
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    target = s_target;
+    mask |= 255u << shift;
+  }
+  const float thr = total_key_to_float(prefix);
+
+  // ---- E: survivors: finite and >= threshold (IEEE), as retain() keeps them (:173)
+  unsigned long long* gbuf = p.sortbuf + (size_t)b * p.sort_cap;
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+  for (int it = 0; it < iters; ++it) {
+    const int i = it * nt + tid;
+    bool keep = false;
+    float s = 0.f;
+    if (i < V) {
+      s = S[i];
+      keep = isfinite(s) && s >= thr;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    int base = 0;
+    if (lane == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (keep) gbuf[base + __popc(bal & ((1u << lane) - 1))] = composite(s, i);
+  }
+  __syncthreads();
+  const int n = s_count;
+
+  // ---- F: sort by (score desc, id asc) (:174)
+  int m = 1;
+  while (m < n) m <<= 1;
+  unsigned long long* srt;
+  if (m <= kSmemSort) {
+    for (int i = tid; i < m; i += nt) srt_s[i] = i < n ? gbuf[i] : ~0ull;
+    __syncthreads();
+    bitonic_sort(srt_s, m);
+    srt = srt_s;
+  } else {
+    for (int i = n + tid; i < m; i += nt) gbuf[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort(gbuf, m);
+    srt = gbuf;
+  }
+
+  // ---- G: top-p, normalisation and the exponential race in warp 0 (:175-213)
+  if (warp != 0) return;
+  float* E = p.expv + (size_t)b * V;
+  auto idof = [&](int i) { return (int)(srt[i] & 0xffffffffu); };
+  const float mx = S[idof(0)];
+  for (int i = lane; i < n; i += 32) E[i] = det_expf(S[idof(i)] - mx);
+  __syncwarp();
+  int nkeep = n;
+  if (c.top_p < 1.f) {
+    if (lane == 0) {
+      float sum = 0.f;
+      for (int i = 0; i < n; ++i) sum += E[i];
+      float cumulative = 0.f;
+      const int protect = legacy ? 3 : 1;
+      int w = 0;
+      for (int i = 0; i < n; ++i) {
+        const float pr = cast(E[i] / sum, legacy);
+        cumulative += pr;
+        const float prior = cast(cast(cumulative, legacy) - pr, legacy);
+        if (prior <= c.top_p || i < protect) {
+          srt[w] = srt[i];
+          E[w] = E[i];
+          ++w;
+        }
+      }
+      s_nkeep = w;
+    }
+    __syncwarp();
+    nkeep = s_nkeep;
+  }
+  if (lane == 0) {
+    float sum = 0.f;
+    for (int i = 0; i < nkeep; ++i) sum += E[i];
+    s_sum = sum;
+  }
+  __syncwarp();
+  const float sum2 = s_sum;
+  const uint32_t* words = p.words + (size_t)b * 2 * V;
+  bool any = false;
+  float bv = 0.f;
+  int bid = 0;
+  for (int i = lane; i < nkeep; i += 32) {
+    const int id = idof(i);
+    const float pr = cast(E[i] / sum2, legacy);
+    const unsigned long long hi = words[2 * id], lo = words[2 * id + 1];
+    const double u = (double)(((hi << 32) | lo) & ((1ull << 53) - 1)) / 9007199254740992.0;
+    const float noise = cast(det_d2f(-det_log1p(-u)), legacy);
+    const float sc = cast(pr / noise, legacy);
+    if (sc == sc && (!any || sc > bv || (sc == bv && id < bid))) {
+      any = true;
+      bv = sc;
+      bid = id;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const int oany = __shfl_xor_sync(0xffffffffu, (int)any, o);
+    const float obv = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int obid = __shfl_xor_sync(0xffffffffu, bid, o);
+    if (oany && (!any || obv > bv || (obv == bv && obid < bid))) {
+      any = true;
+      bv = obv;
+      bid = obid;
+    }
+  }
+  if (lane == 0) finish(0, any ? bid : 0);
+}
+
+cudaError_t launch_sample(cudaStream_t s, bool pdl, const SampleParams& p, int nreq) {
+  SampleParams copy = p;
+  void* args[] = {&copy};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nreq);
+  cfg.blockDim = dim3(kSampleThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, (const void*)sample_kernel, args);
+}
+
+}  // namespace y2
