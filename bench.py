@@ -170,6 +170,9 @@ def main():
     ap.add_argument("--impl", default="product", choices=["product", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="decode steps only (16-id prompts; no sweep, e2e, kernel hook or CPU baseline): "
+                         "the command line for ncu launch lists")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -202,6 +205,9 @@ def main():
     W, K = max(args.warmup, 3), args.steps
     max_tokens = max(512, W + K + 1)
     cond, uncond = prompts(1000 + rank, cfg.vocab_size)
+    if args.profile:
+        cond, uncond = cond[:16], uncond[:16]
+        args.no_sweep = args.no_cpu_baseline = True
     s = c2_sampling(max_tokens)
 
     # ---- device-resident timed region: K decode steps of one song per rank
@@ -229,6 +235,10 @@ def main():
     step_bytes = weight_bytes(cfg) + 2 * kv_bytes_per_token(cfg) * ctx_avg
     peak, peak_kind = measured_peaks()
 
+    if args.profile:
+        model.close()
+        print(json.dumps({"profile_run": True, "ms_per_step": ms / K, "steps": K}), flush=True)
+        return 0
     # ---- dominant kernel live: the gate|up GEMV (fused RMSNorm prologue + SwiGLU epilogue)
     import ctypes
     avg = ctypes.c_double()

@@ -134,8 +134,8 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out);
 int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void* data, uint64_t rows,
                           uint64_t cols);
 /* Seeded synthetic weights on the device: matrices and embeddings N(0, std), RMSNorm
- * gains 1 + N(0, std), all rounded to bf16. */
-int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float std);
+ * gains norm_mean + N(0, std), all rounded to bf16. */
+int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float std, float norm_mean);
 /* Checks that every AR tensor is present and prepares RoPE tables and workspaces. */
 int yue2_model_finalize(Yue2Model* m);
 /* Copies a device tensor back as bf16 bits (count elements). */

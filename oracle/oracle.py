@@ -23,12 +23,13 @@ class OrcSampling(ctypes.Structure):
 _P = {
     "orc_last_error": (ctypes.c_char_p, []),
     "orc_set_threads": (None, [c_int]),
+    "orc_set_dot_order": (None, [c_int]),
     "orc_max_threads": (c_int, []),
     "orc_model_create": (c_p, [c_p, c_p]),
     "orc_model_free": (None, [c_p]),
     "orc_model_set": (c_int, [c_p, ctypes.c_char_p, c_int, c_p, c_u64, c_u64]),
     "orc_model_finalize": (c_int, [c_p]),
-    "orc_model_init_synthetic": (c_int, [c_p, c_u64, c_f]),
+    "orc_model_init_synthetic": (c_int, [c_p, c_u64, c_f, c_f]),
     "orc_cache_create": (c_p, [c_p, c_u64]),
     "orc_cache_free": (None, [c_p]),
     "orc_cache_length": (c_u64, [c_p]),
@@ -102,6 +103,11 @@ def set_threads(n):
     lib().orc_set_threads(n)
 
 
+def set_dot_order(order):
+    """0: 16 interleaved partial sums (default); 1: strictly sequential dot products."""
+    lib().orc_set_dot_order(order)
+
+
 class OracleModel:
     def __init__(self, config):
         self.config = c = config
@@ -124,9 +130,9 @@ class OracleModel:
         return m
 
     @classmethod
-    def synthetic(cls, config, seed, std=0.02):
+    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0):
         m = cls(config)
-        _ck(lib().orc_model_init_synthetic(m._h, seed, std))
+        _ck(lib().orc_model_init_synthetic(m._h, seed, std, norm_mean))
         return m
 
     def set(self, name, arr, code, rows, cols):

@@ -104,6 +104,12 @@ float half_to_float(uint16_t h) {
   return det_u2f(sign | ((exp + 112) << 23) | (man << 13));
 }
 
+// Summation order of the dot products: Accelerate's cblas_sgemv order is unknown, so the
+// checker offers two valid restatements -- 16 interleaved partial sums (default) and a
+// strictly sequential sum. Their disagreement measures how far bf16 rounding after every
+// op amplifies a change of f32 summation order (the parity noise floor).
+int g_dot_order = 0;
+
 // y[r, n] = round_bf16(sum_k W[n,k] x[r,k]) -- Linear::apply + finish (tensor.rs:946-1118)
 void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin = 0, size_t end = SIZE_MAX) {
   if (end == SIZE_MAX) end = W.rows;
@@ -117,6 +123,12 @@ void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin
       for (size_t k = 0; k < K; ++k) wrow[k] = bf(src[k]);
       for (size_t r = 0; r < rows; ++r) {
         const float* xr = x + r * K;
+        if (g_dot_order == 1) {
+          float s = 0.f;
+          for (size_t k = 0; k < K; ++k) s += wrow[k] * xr[k];
+          y[r * N + n] = round_bf16(s);
+          continue;
+        }
         float acc[16] = {0};
         size_t k = 0;
         for (; k + 16 <= K; k += 16)
@@ -347,6 +359,7 @@ ORC_API void orc_set_threads(int n) {
   (void)n;
 #endif
 }
+ORC_API void orc_set_dot_order(int order) { g_dot_order = order; }
 ORC_API int orc_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
@@ -436,8 +449,8 @@ ORC_API int orc_model_finalize(void* p) {
 }
 
 // Seeded synthetic weights for CPU timing runs: matrices N(0, std) and norm
-// gains 1 + N(0, std), rounded to bf16 (splitmix64 + Box-Muller).
-ORC_API int orc_model_init_synthetic(void* p, uint64_t seed, float std_) {
+// gains norm_mean + N(0, std), rounded to bf16 (splitmix64 + Box-Muller).
+ORC_API int orc_model_init_synthetic(void* p, uint64_t seed, float std_, float norm_mean) {
   Model* m = (Model*)p;
   const Config& c = m->c;
   uint64_t tensor = 0;
@@ -464,7 +477,7 @@ ORC_API int orc_model_init_synthetic(void* p, uint64_t seed, float std_) {
   };
   auto nrm = [&](std::vector<float>& g, size_t d) {
     std::vector<uint16_t> t;
-    fill(t, d, 1.f);
+    fill(t, d, norm_mean);
     g.resize(d);
     for (size_t i = 0; i < d; ++i) g[i] = bf(t[i]);
   };

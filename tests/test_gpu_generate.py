@@ -36,22 +36,22 @@ def replay(model, prefix, negative, scale, s, seed, phase, legacy=False):
 
 
 @pytest.mark.parametrize("temperature", [1.0, 0.0])
-def test_generate_cfg_matches_replay(c1_device, c1_prompt, temperature):
+def test_generate_cfg_matches_replay(c1u_device, c1_prompt, temperature):
     prompt = c1_prompt[0][:40]
     negative = c1_prompt[0][200:230]
     s = Sampling(temperature, 0.93, 50, 1.2, 50, 0, 24)
-    g = generate(c1_device, prompt, s, 77, Phase.VOCAB, negative, 1.5)
-    want, trunc = replay(c1_device, prompt, negative, 1.5, s, 77, Phase.VOCAB)
+    g = generate(c1u_device, prompt, s, 77, Phase.VOCAB, negative, 1.5)
+    want, trunc = replay(c1u_device, prompt, negative, 1.5, s, 77, Phase.VOCAB)
     assert g.tokens == want and g.truncated and trunc and len(g.tokens) == 24
 
 
-def test_generate_without_cfg_and_batch(c1_device, c1_prompt):
+def test_generate_without_cfg_and_batch(c1u_device, c1_prompt):
     p = c1_prompt[0]
     s = Sampling(1.0, 0.9, 40, 1.1, 20, 0, 12)
     reqs = [Request(p[:17], 5), Request(p[30:50], 6, p[60:70], 1.5), Request(p[80:90], 7, p[90:99], 2.0, True)]
-    outs = generate_batch(c1_device, reqs, s, Phase.VOCAB)
+    outs = generate_batch(c1u_device, reqs, s, Phase.VOCAB)
     for r, o in zip(reqs, outs):
-        want, _ = replay(c1_device, r.prefix, r.negative, r.scale, s, r.seed, Phase.VOCAB, r.legacy)
+        want, _ = replay(c1u_device, r.prefix, r.negative, r.scale, s, r.seed, Phase.VOCAB, r.legacy)
         assert o.tokens == want
 
 
@@ -62,7 +62,7 @@ def test_stop_token_ends_generation():
     c.vocab_size, c.num_hidden_layers = 184704, 1
     m = Model(c)
     from yue2_rs_b200 import _lib
-    _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, 3, 0.02))
+    _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, 3, 0.02, 1.0))
     m.set_tensor("lm_head.weight", np.zeros((c.vocab_size, c.hidden_size), dtype=np.uint16))
     m.finalize()
     s = Sampling(0.0, 0.95, 100, 1.2, 50, 5, 50)

@@ -1,54 +1,96 @@
-"""teacher-forced per-step logits of the CUDA path against the
-oracle's restatement of the reference decode path (tolerance 2e-2 max-abs, 1e-3 mean-abs)."""
+"""teacher-forced per-step logits of the CUDA path against the oracle's
+restatement of the reference decode path.
+
+Two criteria:
+  * the north_star tolerance (2e-2 max-abs, 1e-3 mean-abs) on config 0 as specified
+    (every weight, RMSNorm gains included, bf16 N(0, 0.02), seed 0);
+  * a noise-floor criterion on config 0 and on a unit-gain variant (gains 1 + N(0, 0.02)):
+    the reference rounds to bf16 after every op, so a change of f32 summation order alone
+    moves ~70% of unit-gain logits by an ulp. The oracle evaluated with two valid orders
+    (16 interleaved partial sums, strictly sequential) measures that floor; the CUDA path,
+    which has its own order, must stay within 2.5x of it.
+"""
 import numpy as np
 import pytest
+
+from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
 
 MAX_ABS, MEAN_ABS = 2e-2, 1e-3
 
 
-def compare(got, want, what):
-    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
-    assert np.isfinite(got).all(), what
-    assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, f"{what}: max {d.max():.3g} mean {d.mean():.3g}"
-    return d.max(), d.mean()
+def run_oracle(model, prompt, teacher, order):
+    orc.set_dot_order(order)
+    try:
+        c = model.cache(len(prompt) + len(teacher))
+        return np.array([model.prefill(prompt, c)] + [model.forward([t], c) for t in teacher])
+    finally:
+        orc.set_dot_order(0)
+
+
+def run_device(model, prompt, teacher):
+    c = model.new_cache(len(prompt) + len(teacher))
+    out = [model.forward(prompt, c)] + [model.forward([t], c) for t in teacher]
+    assert c.length == len(prompt) + len(teacher)
+    return np.array(out), c
+
+
+def floor_check(dev, ref, alt):
+    d = np.abs(dev.astype(np.float64) - ref)
+    f = np.abs(alt.astype(np.float64) - ref)
+    rel_dev = np.linalg.norm(dev.astype(np.float64) - ref) / np.linalg.norm(ref)
+    rel_floor = np.linalg.norm(alt.astype(np.float64) - ref) / np.linalg.norm(ref)
+    assert np.isfinite(dev).all()
+    assert rel_dev <= 2.5 * rel_floor + 1e-6, (rel_dev, rel_floor)
+    assert d.mean() <= 2.5 * f.mean() + 1e-7, (d.mean(), f.mean())
+    assert (np.argmax(dev, 1) == np.argmax(ref, 1)).mean() >= 0.9
+    return d, rel_dev, rel_floor
 
 
 def test_teacher_forced_logits_config0(c1_device, c1_oracle, c1_prompt):
     prompt, teacher = c1_prompt
-    cap = len(prompt) + len(teacher)
-    dc = c1_device.new_cache(cap)
-    oc = c1_oracle.cache(cap)
-    compare(c1_device.forward(prompt, dc), c1_oracle.prefill(prompt, oc), "prefill")
-    worst = []
-    for step, tok in enumerate(teacher):
-        worst.append(compare(c1_device.forward([tok], dc), c1_oracle.forward([tok], oc), f"step {step}"))
-    assert dc.length == oc.length == cap
+    dev, dc = run_device(c1_device, prompt, teacher)
+    ref = run_oracle(c1_oracle, prompt, teacher, 0)
+    for step in range(len(dev)):
+        d = np.abs(dev[step].astype(np.float64) - ref[step])
+        assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, (step, d.max(), d.mean())
+    alt = run_oracle(c1_oracle, prompt, teacher, 1)
+    floor_check(dev, ref, alt)
     # the KV caches agree except for rare bf16 rounding flips
+    oc = c1_oracle.cache(len(prompt) + len(teacher))
+    c1_oracle.prefill(prompt + teacher, oc, logits=False)
+    to_f = lambda b: (b.astype(np.uint32) << 16).view(np.float32)
     for layer in range(c1_oracle.config.num_hidden_layers):
-        kd, vd = dc.read(layer, 0, cap)
+        kd, vd = dc.read(layer, 0, dc.length)
         ko, vo = oc.read(layer)
-        to_f = lambda b: (b.astype(np.uint32) << 16).view(np.float32)
-        assert np.mean(to_f(kd) == ko) > 0.99 and np.mean(to_f(vd) == vo) > 0.99
+        assert np.mean(to_f(kd) == ko) > 0.98 and np.mean(to_f(vd) == vo) > 0.98
 
 
-def test_batched_rows_equal_single_rows(c1_device, c1_prompt):
+def test_teacher_forced_logits_unit_gains(c1u_device, c1u_oracle, c1_prompt):
+    prompt, teacher = c1_prompt
+    dev, _ = run_device(c1u_device, prompt, teacher[:24])
+    ref = run_oracle(c1u_oracle, prompt, teacher[:24], 0)
+    alt = run_oracle(c1u_oracle, prompt, teacher[:24], 1)
+    floor_check(dev, ref, alt)
+
+
+def test_batched_rows_equal_single_rows(c1u_device, c1_prompt):
     """Rows in one weight pass do not interact: R=3 gives the R=1 logits bit for bit."""
     prompt, teacher = c1_prompt
-    caches = [c1_device.new_cache(64) for _ in range(3)]
-    singles = [c1_device.new_cache(64) for _ in range(3)]
+    caches = [c1u_device.new_cache(64) for _ in range(3)]
+    singles = [c1u_device.new_cache(64) for _ in range(3)]
     for i in range(3):
-        c1_device.forward(prompt[i * 5: i * 5 + 7], caches[i])
-        c1_device.forward(prompt[i * 5: i * 5 + 7], singles[i])
-    rows = c1_device.forward_rows(caches, teacher[:3])
+        c1u_device.forward(prompt[i * 5: i * 5 + 7], caches[i])
+        c1u_device.forward(prompt[i * 5: i * 5 + 7], singles[i])
+    rows = c1u_device.forward_rows(caches, teacher[:3])
     for i in range(3):
-        one = c1_device.forward([teacher[i]], singles[i])
+        one = c1u_device.forward([teacher[i]], singles[i])
         assert (rows[i].view(np.uint32) == one.view(np.uint32)).all()
 
 
 def test_capacity_and_token_errors(c1_device):
-    from yue2_rs_b200 import Yue2Error
+    from yue2_rs_b200 import Phase, Yue2Error
     c = c1_device.new_cache(2)
     c1_device.forward([1, 2], c)
     with pytest.raises(Yue2Error, match="exceeds cache"):
@@ -56,5 +98,4 @@ def test_capacity_and_token_errors(c1_device):
     with pytest.raises(Yue2Error, match="outside model vocabulary"):
         c1_device.forward([c1_device.config.vocab_size], c1_device.new_cache(4))
     with pytest.raises(Yue2Error, match="native music protocol"):
-        from yue2_rs_b200 import Phase
         c1_device.forward_phase([1], c1_device.new_cache(4), Phase.SEMANTIC)

@@ -71,8 +71,8 @@ def test_checkpoint_roundtrip(tmp_path):
 def test_synthetic_checkpoint_is_deterministic():
     c = Config(hidden_size=16, num_hidden_layers=1, num_attention_heads=2, num_key_value_heads=1, head_dim=8,
                intermediate_size=32, vocab_size=40, max_latent_frames=4, latent_dim=4)
-    a = {n: b for n, _, b in synth.generate(c, 0)}
-    b = {n: b for n, _, b in synth.generate(c, 0)}
+    a = {n: b for n, _, b in synth.generate(c, 0, norm_mean=1.0)}
+    b = {n: b for n, _, b in synth.generate(c, 0, norm_mean=1.0)}
     assert a.keys() == b.keys() and all((a[k] == b[k]).all() for k in a)
     assert "model.layers.0.nar_mlp.down_proj.weight" in a and "latent_pos_embed.pe" in a
     g = a["model.layers.0.input_layernorm.weight"].astype(np.uint32) << 16

@@ -25,7 +25,7 @@ def test_logits_are_bf16_valued_and_finite(c1_oracle, c1_prompt):
     x = c1_oracle.prefill(c1_prompt[0][:8], c)
     assert np.isfinite(x).all()
     assert (x.view(np.uint32) & 0xFFFF == 0).all()
-    assert 0.3 < float(np.std(x)) < 5.0
+    assert 0.003 < float(np.std(x)) < 0.1  # config 0: every weight N(0, 0.02), gains included
 
 
 def test_capacity_token_and_phase_errors(c1_oracle):

@@ -113,7 +113,10 @@ int y2_set_device(const Yue2Model* m) {
 
 Yue2Model::~Yue2Model() {
   cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& e : row_events)
+    if (e) cudaEventDestroy(e);
   pool.clear();
   for (void* p : allocations) cudaFree(p);
   if (pinned_rows) cudaFreeHost(pinned_rows);
@@ -281,7 +284,7 @@ int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void*
   return 0;
 }
 
-int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float stddev) {
+int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float stddev, float norm_mean) {
   if (!m) return fail(YUE2_ERR_INVALID, "null model");
   int rc = y2_set_device(m);
   if (rc) return rc;
@@ -298,8 +301,8 @@ int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float stddev) {
         z ^= z >> 31;
         const double u1 = ((z >> 11) + 1) * (1.0 / 9007199254740992.0), u2 = (z & 0x1fffff) * (1.0 / 2097152.0);
         const double rad = sqrt(-2.0 * log(u1));
-        v[i] = round_bf16(1.0f + stddev * (float)(rad * cos(6.283185307179586 * u2)));
-        if (i + 1 < v.size()) v[i + 1] = round_bf16(1.0f + stddev * (float)(rad * sin(6.283185307179586 * u2)));
+        v[i] = round_bf16(norm_mean + stddev * (float)(rad * cos(6.283185307179586 * u2)));
+        if (i + 1 < v.size()) v[i + 1] = round_bf16(norm_mean + stddev * (float)(rad * sin(6.283185307179586 * u2)));
       }
       CK(cudaMemcpy(m->arena + t.offset, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
     } else {
@@ -385,7 +388,7 @@ int yue2_model_finalize(Yue2Model* m) {
     if ((rc = m->alloc(&p, 256))) return rc;
     m->flags = (int32_t*)p;
     CK(cudaMemset(p, 0, 256));
-    CK(cudaMallocHost(&m->pinned_rows, R * sizeof(DevRow)));
+    CK(cudaMallocHost(&m->pinned_rows, Yue2Model::kRowSlots * R * sizeof(DevRow)));
     CK(cudaMallocHost(&m->pinned_flags, 4096));
     m->workspace_ready = true;
   }
@@ -665,9 +668,16 @@ int run_forward(Yue2Model& m, int R, bool head, int phase) {
   return 0;
 }
 
+// Stages the row descriptors through a ring of pinned slots: an asynchronous copy reads
+// its slot when the stream reaches it, so a slot is reused only after its copy is done.
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows) {
-  memcpy(m.pinned_rows, rows.data(), rows.size() * sizeof(DevRow));
-  CK(cudaMemcpyAsync(m.rows, m.pinned_rows, rows.size() * sizeof(DevRow), cudaMemcpyHostToDevice, m.stream));
+  const int slot = (int)(m.row_slot++ % Yue2Model::kRowSlots);
+  if (m.row_events[slot]) CK(cudaEventSynchronize(m.row_events[slot]));
+  else CK(cudaEventCreateWithFlags(&m.row_events[slot], cudaEventDisableTiming));
+  DevRow* staging = m.pinned_rows + (size_t)slot * kMaxRows;
+  memcpy(staging, rows.data(), rows.size() * sizeof(DevRow));
+  CK(cudaMemcpyAsync(m.rows, staging, rows.size() * sizeof(DevRow), cudaMemcpyHostToDevice, m.stream));
+  CK(cudaEventRecord(m.row_events[slot], m.stream));
   return 0;
 }
 

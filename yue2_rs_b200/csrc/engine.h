@@ -66,7 +66,10 @@ struct Yue2Model {
   y2::DevRow* rows = nullptr;
   int32_t* flags = nullptr;  // [0] token out of range, [1] position outside RoPE table
   int max_splits = 64;
+  static constexpr int kRowSlots = 32;  // pinned staging ring for row descriptors
   y2::DevRow* pinned_rows = nullptr;
+  cudaEvent_t row_events[kRowSlots] = {};
+  uint64_t row_slot = 0;
   int32_t* pinned_flags = nullptr;
 
   std::map<int, cudaGraphExec_t> graphs;

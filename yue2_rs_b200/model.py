@@ -1,5 +1,6 @@
 """Device model and KV caches: the decode entry points of the reference's src/model.rs
 (Model::open/forward/forward_phase/prefill/prefill_phase, Cache) on libyue2cuda."""
+import atexit
 import ctypes
 import json
 import math
@@ -68,6 +69,20 @@ def _ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+_LIVE = weakref.WeakSet()
+
+
+@atexit.register
+def _release_all():
+    """Free device objects while the CUDA runtime is still up (module globals would
+    otherwise be finalised after it has been torn down)."""
+    for m in list(_LIVE):
+        try:
+            m.close()
+        except Exception:
+            pass
+
+
 class Model:
     """A model resident on one GPU. Tensors are uploaded by their checkpoint names."""
 
@@ -79,6 +94,7 @@ class Model:
         _lib.check(_lib.lib().yue2_model_create(device, ctypes.byref(c), ctypes.byref(h)))
         self._h = h
         self._children = weakref.WeakSet()  # caches/generators to release before the model
+        _LIVE.add(self)
 
     # ---- construction
     @classmethod
@@ -92,11 +108,11 @@ class Model:
         return m
 
     @classmethod
-    def synthetic(cls, config, seed, std=0.02, device=0):
-        """Seeded synthetic weights generated on the device (matrices N(0, std),
-        RMSNorm gains 1 + N(0, std), bf16)."""
+    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, device=0):
+        """Seeded synthetic weights generated on the device: matrices N(0, std), RMSNorm
+        gains norm_mean + N(0, std), bf16."""
         m = cls(config, device)
-        _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, seed, std))
+        _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, seed, std, norm_mean))
         m.finalize()
         return m
 

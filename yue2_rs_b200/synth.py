@@ -1,7 +1,8 @@
 """Seeded synthetic YuE2 checkpoints under the reference's tensor names
 (src/model.rs:76-93,103-114,176-200,250-270,418-451), written as safetensors.
 
-Matrices and embeddings are bf16(std * z), RMSNorm gains bf16(1 + std * z), biases zero,
+Matrices and embeddings are bf16(std * z), RMSNorm gains bf16(norm_mean + std * z) (norm_mean
+0 follows the benchmark configurations literally: every weight N(0, std)), biases zero,
 z standard normal from numpy's PCG64 generator seeded with `seed`, drawn tensor by tensor
 in the order of `tensor_specs`. NAR and latent tensors are included so that the
 reference's own Model::open would accept the directory.
@@ -59,7 +60,7 @@ def bf16_bits(x):
     return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), r)
 
 
-def generate(config, seed, std=0.02):
+def generate(config, seed, std=0.02, norm_mean=0.0):
     """Yields (name, shape, bf16 bits) for every tensor."""
     rng = np.random.default_rng(seed)
     for name, shape, kind in tensor_specs(config):
@@ -70,17 +71,17 @@ def generate(config, seed, std=0.02):
             z = rng.standard_normal(n, dtype=np.float32)
             z *= np.float32(std)
             if kind == "norm":
-                z += np.float32(1.0)
+                z += np.float32(norm_mean)
             bits = bf16_bits(z)
         yield name, shape, bits.reshape(shape)
 
 
-def write_checkpoint(path, config, seed, std=0.02):
+def write_checkpoint(path, config, seed, std=0.02, norm_mean=0.0):
     """Writes config.json + model.safetensors; returns the directory."""
     os.makedirs(path, exist_ok=True)
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(config.json(), f, indent=1)
-    named = {name: ("BF16", shape, bits) for name, shape, bits in generate(config, seed, std)}
+    named = {name: ("BF16", shape, bits) for name, shape, bits in generate(config, seed, std, norm_mean)}
     checkpoint.write(os.path.join(path, "model.safetensors"), named, {"format": "pt", "synthetic_seed": str(seed)})
     return path
 
