@@ -345,7 +345,7 @@ int yue2_cuda_vector(const float* input, const uint8_t* raw, size_t mapping, int
   std::lock_guard<std::mutex> lock(d.mu);
   if (!ensure_init(d)) return 0;
   if (!input || !raw || !out || rows == 0 || cols == 0) return fail(0, "null argument or empty shape");
-  if (cols % 8 || rows > 0x7fffffff || cols > 65536) return fail(0, "cols must be a multiple of 8 (<= 65536)");
+  if (cols % 8 || rows > 0x7fffffff || cols > 32768) return fail(0, "cols must be a multiple of 8 (<= 32768)");
   if (!ok_or(cudaSetDevice(d.device), "cudaSetDevice")) return 0;
   uint16_t* w = weight(d, raw, mapping, rows, cols, dtype, rounded);
   if (!w) return 0;
@@ -369,7 +369,7 @@ int yue2_cuda_vector(const float* input, const uint8_t* raw, size_t mapping, int
   p.xf = d.vec_in;
   p.of = d.vec_out;
   p.ldo = (int)rows;
-  if (!ok_or(launch_gemv(d.stream, false, kXF32, kEpiRawF32, p, d.sms), "weight_vector launch")) return 0;
+  if (!ok_or(launch_gemv(d.stream, false, kXF32, kEpiRawF32, p, 2 * d.sms), "weight_vector launch")) return 0;
   if (!ok_or(cudaMemcpyAsync(out, d.vec_out, rows * 4, cudaMemcpyDeviceToHost, d.stream), "output copy")) return 0;
   return ok_or(cudaStreamSynchronize(d.stream), "weight_vector");
 }
@@ -472,7 +472,7 @@ int yue2_cuda_ar_stack(const float* input, float* out, float* shadow, const Yue2
              "rows") ||
       !ok_or(cudaMemcpyAsync(d.x, input, hidden * 4, cudaMemcpyHostToDevice, d.stream), "input"))
     return 0;
-  const int grid = d.sms;
+  const int grid = 2 * d.sms;
   for (size_t l = 0; l < count; ++l) {
     GemvParams p = {};
     p.w[0] = w[l].q;

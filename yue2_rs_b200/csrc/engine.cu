@@ -248,7 +248,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     delete m;
     return cuda_fail(e, "stream/event creation");
   }
-  m->gemv_grid = m->sms * std::max(1, env_int("YUE2_CUDA_GEMV_CTAS_PER_SM", 1));
+  m->gemv_grid = m->sms * std::max(1, env_int("YUE2_CUDA_GEMV_CTAS_PER_SM", 2));
   m->use_pdl = env_int("YUE2_CUDA_PDL", 1) != 0;
   m->use_graphs = env_int("YUE2_CUDA_GRAPHS", 1) != 0;
   *out = m;

@@ -120,12 +120,23 @@ Y2_DEV float block_sum(float v, float* red) {
   return t;
 }
 
-template <int RM, bool PAIR, int XM, int EPI, int CH>
-__global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvParams p) {
+// Weight stream: every thread owns 16-byte chunks of its warp's current row and copies
+// them with cp.async.cg (L2 only) into its own slots of a kStages-deep shared-memory
+// ring, kStages-1 batches ahead of the batch it multiplies. A thread reads back only
+// what it copied itself, so the hardware cp.async.wait_group is the only wait (no
+// barrier, no spin). The first kStages-1 batches are requested before
+// griddepcontrol.wait: they stream while the previous kernel drains.
+constexpr int kGemvThreads = 256;
+constexpr int kStages = 4;
+
+template <int RM, bool PAIR, int XM, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float red[32];
   constexpr int NP = PAIR ? 2 : 1;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  constexpr int CH = PAIR ? 2 : 4;  // chunks per lane per batch and matrix
+  constexpr int NT = kGemvThreads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = NT / 32;
   const int K = p.K, K8 = K >> 3;
   const int nb = (K8 + 32 * CH - 1) / (32 * CH);
   const int row_begin = (int)(((long long)p.N * blockIdx.x) / gridDim.x);
@@ -133,62 +144,67 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvParams p) {
   const int first = row_begin + warp;
   const int nrows_w = first < row_end ? (row_end - first + nwarps - 1) / nwarps : 0;
   const int T = nrows_w * nb;
+  uint4* ring = reinterpret_cast<uint4*>(smem_raw);  // [kStages][NP][CH][NT]
+  unsigned char* xbase = smem_raw + (size_t)kStages * NP * CH * NT * 16;
 
   auto wrow = [&](int n) -> const uint16_t* {
     const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
     return p.w[s] + (size_t)(n - p.seg_start[s]) * K;
   };
-  auto load = [&](uint4(&buf)[NP][CH], int t) {
-    const int n = first + (t / nb) * nwarps, b = t % nb;
-    const uint16_t* w0 = wrow(n);
-    const uint16_t* w1 = PAIR ? p.wpair + (size_t)n * K : nullptr;
+  auto issue = [&](int t) {
+    if (t < T) {
+      const int n = first + (t / nb) * nwarps, b = t % nb;
+      const uint16_t* w0 = wrow(n);
+      const uint16_t* w1 = PAIR ? p.wpair + (size_t)n * K : nullptr;
+      uint4* st = ring + (size_t)(t % kStages) * NP * CH * NT;
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int idx = (b * CH + c) * 32 + lane;
-      if (idx < K8) {
-        buf[0][c] = ldg_stream(w0 + (size_t)idx * 8);
-        if (PAIR) buf[NP - 1][c] = ldg_stream(w1 + (size_t)idx * 8);
-      } else {
-        buf[0][c] = make_uint4(0, 0, 0, 0);
-        if (PAIR) buf[NP - 1][c] = make_uint4(0, 0, 0, 0);
+      for (int c = 0; c < CH; ++c) {
+        const int idx = (b * CH + c) * 32 + lane;
+        if (idx < K8) {
+          cp_async16(st + c * NT + tid, w0 + (size_t)idx * 8);
+          if (PAIR) cp_async16(st + (CH + c) * NT + tid, w1 + (size_t)idx * 8);
+        }
       }
     }
+    cp_async_commit();  // one group per batch, empty past the end, so counts stay aligned
   };
 
-  uint4 A[NP][CH], B[NP][CH];
-  if (T > 0) load(A, 0);
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) issue(t);
 
   pdl_wait();
   pdl_trigger();
-  if (p.skip && *p.skip) return;
+  if (p.skip && *p.skip) {
+    cp_async_wait<0>();
+    return;
+  }
 
   // ---- stage activations
   if (XM == kXF32) {
-    float* xs = reinterpret_cast<float*>(smem_raw);
-    for (int i = threadIdx.x; i < RM * K; i += blockDim.x) {
+    float* xs = reinterpret_cast<float*>(xbase);
+    for (int i = tid; i < RM * K; i += NT) {
       const int r = i / K;
       xs[i] = r < p.R ? p.xf[i] : 0.f;
     }
   } else if (XM == kXBf16) {
-    uint4* xs = reinterpret_cast<uint4*>(smem_raw);
-    for (int i = threadIdx.x; i < RM * K8; i += blockDim.x) {
+    uint4* xs = reinterpret_cast<uint4*>(xbase);
+    for (int i = tid; i < RM * K8; i += NT) {
       const int r = i / K8;
       xs[i] = r < p.R ? ldg16(p.xb + (size_t)i * 8) : make_uint4(0, 0, 0, 0);
     }
   } else {  // kXNorm: RMSNorm of the f32 residual, bf16 rounded as Norm::apply does
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem_raw);
+    uint16_t* xs = reinterpret_cast<uint16_t*>(xbase);
     for (int r = 0; r < RM; ++r) {
       if (r >= p.R) {
-        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[r * K + i] = 0;
+        for (int i = tid; i < K; i += NT) xs[r * K + i] = 0;
         continue;
       }
       const float* xr = p.xf + (size_t)r * K;
       float ss = 0.f;
-      for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+      for (int i = tid; i < K; i += NT) ss = fmaf(xr[i], xr[i], ss);
       ss = block_sum(ss, red);
       const float scale = round_bf16(1.0f / sqrtf(ss / (float)K + p.eps));
-      for (int i = threadIdx.x; i < K; i += blockDim.x)
-        xs[r * K + i] = f2bf_exact(round_bf16(round_bf16(xr[i] * scale) * p.gamma[i]));
+      for (int i = tid; i < K; i += NT) xs[r * K + i] = f2bf_exact(round_bf16(round_bf16(xr[i] * scale) * p.gamma[i]));
     }
   }
   __syncthreads();
@@ -233,90 +249,83 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvParams p) {
       for (int r = 0; r < RM; ++r) acc[q][r] = 0.f;
   };
 
-  auto compute = [&](const uint4(&buf)[NP][CH], int t) {
+  for (int t = 0; t < T; ++t) {
+    cp_async_wait<kStages - 2>();  // this thread's batch t has landed
+    const uint4* st = ring + (size_t)(t % kStages) * NP * CH * NT;
     const int b = t % nb;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int idx = (b * CH + c) * 32 + lane;
       if (idx < K8) {
+        uint4 w[NP];
+#pragma unroll
+        for (int q = 0; q < NP; ++q) w[q] = st[(q * CH + c) * NT + tid];
 #pragma unroll
         for (int r = 0; r < RM; ++r) {
           if (XM == kXF32) {
-            const float4* xs = reinterpret_cast<const float4*>(smem_raw) + ((size_t)r * K8 + idx) * 2;
+            const float4* xs = reinterpret_cast<const float4*>(xbase) + ((size_t)r * K8 + idx) * 2;
             const float4 a = xs[0], bb = xs[1];
 #pragma unroll
-            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_f32(buf[q][c], a, bb, acc[q][r]);
+            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_f32(w[q], a, bb, acc[q][r]);
           } else {
-            const uint4 xv = reinterpret_cast<const uint4*>(smem_raw)[(size_t)r * K8 + idx];
+            const uint4 xv = reinterpret_cast<const uint4*>(xbase)[(size_t)r * K8 + idx];
 #pragma unroll
-            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_bf(buf[q][c], xv, acc[q][r]);
+            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_bf(w[q], xv, acc[q][r]);
           }
         }
       }
     }
     if (b == nb - 1) finish(first + (t / nb) * nwarps);
-  };
-
-  for (int t = 0; t < T; t += 2) {
-    if (t + 1 < T) load(B, t + 1);
-    compute(A, t);
-    if (t + 1 >= T) break;
-    if (t + 2 < T) load(A, t + 2);
-    compute(B, t + 1);
+    issue(t + kStages - 1);  // refills the slot batch t-1 used
   }
+  cp_async_wait<0>();
 }
 
 size_t gemv_smem_bytes(int xmode, int K, int R) {
   const int rm = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
-  return (size_t)rm * K * (xmode == kXF32 ? 4 : 2);
+  return (size_t)kStages * 4 * kGemvThreads * 16 + (size_t)rm * K * (xmode == kXF32 ? 4 : 2);
 }
 
-template <int RM, bool PAIR, int XM, int EPI, int CH>
+constexpr int kMaxSmem = 227 * 1024 - 1024;  // opt-in limit minus room for static shared memory
+
+template <int RM, bool PAIR, int XM, int EPI>
 static cudaError_t gemv_go(cudaStream_t s, bool pdl, const GemvParams& p, int grid) {
-  const void* fn = (const void*)gemv_kernel<RM, PAIR, XM, EPI, CH>;
-  const size_t smem = (size_t)RM * p.K * XTraits<XM>::bytes;
-  cudaError_t e = ensure_smem_attr(fn, 200 * 1024);
+  const void* fn = (const void*)gemv_kernel<RM, PAIR, XM, EPI>;
+  const size_t smem = (size_t)kStages * 4 * kGemvThreads * 16 + (size_t)RM * p.K * XTraits<XM>::bytes;
+  if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
+  cudaError_t e = ensure_smem_attr(fn, kMaxSmem);
   if (e != cudaSuccess || g_configure_only) return e;
   GemvParams copy = p;
   void* args[] = {&copy};
-  return launch_with(s, pdl, dim3(grid), dim3(256), smem, fn, args);
+  return launch_with(s, pdl, dim3(grid), dim3(kGemvThreads), smem, fn, args);
 }
 
-template <bool PAIR, int XM, int EPI, int CH>
+template <bool PAIR, int XM, int EPI>
 static cudaError_t gemv_rows(cudaStream_t s, bool pdl, const GemvParams& p, int grid) {
-  if (p.R <= 1) return gemv_go<1, PAIR, XM, EPI, CH>(s, pdl, p, grid);
-  if (p.R <= 2) return gemv_go<2, PAIR, XM, EPI, CH>(s, pdl, p, grid);
-  if (p.R <= 4) return gemv_go<4, PAIR, XM, EPI, CH>(s, pdl, p, grid);
-  return gemv_go<8, PAIR, XM, EPI, CH>(s, pdl, p, grid);
+  if (p.R <= 1) return gemv_go<1, PAIR, XM, EPI>(s, pdl, p, grid);
+  if (p.R <= 2) return gemv_go<2, PAIR, XM, EPI>(s, pdl, p, grid);
+  if (p.R <= 4) return gemv_go<4, PAIR, XM, EPI>(s, pdl, p, grid);
+  return gemv_go<8, PAIR, XM, EPI>(s, pdl, p, grid);
 }
 
 cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
   if (p.R < 1 || p.R > kMaxRows || (p.K & 7) || p.N < 1) return cudaErrorInvalidValue;
-  const int K8 = p.K >> 3;
-  // chunks per lane per batch: whole batches where the row length allows it
-  const bool c8 = (K8 % 256) == 0, c6 = (K8 % 192) == 0;
   switch (epi) {
     case kEpiBf16:
-      if (xmode == kXNorm) return c8 ? gemv_rows<false, kXNorm, kEpiBf16, 8>(s, pdl, p, grid)
-                                : c6 ? gemv_rows<false, kXNorm, kEpiBf16, 6>(s, pdl, p, grid)
-                                     : gemv_rows<false, kXNorm, kEpiBf16, 4>(s, pdl, p, grid);
+      if (xmode == kXNorm) return gemv_rows<false, kXNorm, kEpiBf16>(s, pdl, p, grid);
       break;
     case kEpiResidual:
-      if (xmode == kXBf16) return c8 ? gemv_rows<false, kXBf16, kEpiResidual, 8>(s, pdl, p, grid)
-                                : c6 ? gemv_rows<false, kXBf16, kEpiResidual, 6>(s, pdl, p, grid)
-                                     : gemv_rows<false, kXBf16, kEpiResidual, 4>(s, pdl, p, grid);
+      if (xmode == kXBf16) return gemv_rows<false, kXBf16, kEpiResidual>(s, pdl, p, grid);
       break;
     case kEpiSwiGLU:
-      if (xmode == kXNorm) return gemv_rows<true, kXNorm, kEpiSwiGLU, 4>(s, pdl, p, grid);
+      if (xmode == kXNorm) return gemv_rows<true, kXNorm, kEpiSwiGLU>(s, pdl, p, grid);
       break;
     case kEpiLogits:
-      if (xmode == kXNorm) return c8 ? gemv_rows<false, kXNorm, kEpiLogits, 8>(s, pdl, p, grid)
-                                : c6 ? gemv_rows<false, kXNorm, kEpiLogits, 6>(s, pdl, p, grid)
-                                     : gemv_rows<false, kXNorm, kEpiLogits, 4>(s, pdl, p, grid);
-      if (xmode == kXBf16) return gemv_rows<false, kXBf16, kEpiLogits, 4>(s, pdl, p, grid);
+      if (xmode == kXNorm) return gemv_rows<false, kXNorm, kEpiLogits>(s, pdl, p, grid);
+      if (xmode == kXBf16) return gemv_rows<false, kXBf16, kEpiLogits>(s, pdl, p, grid);
       break;
     case kEpiRawF32:
-      if (xmode == kXF32 && p.R == 1) return gemv_go<1, false, kXF32, kEpiRawF32, 4>(s, pdl, p, grid);
+      if (xmode == kXF32 && p.R == 1) return gemv_go<1, false, kXF32, kEpiRawF32>(s, pdl, p, grid);
       break;
   }
   return cudaErrorInvalidValue;

@@ -102,12 +102,13 @@ Y2_DEV void bitonic_sort(T* a, int m) {
     }
 }
 
-constexpr int kSmemSort = 2048;
+constexpr int kCand = 2048;  // candidates / survivors sorted in shared memory
 constexpr int kSampleThreads = 1024;
+constexpr int kHistBits = 12;  // first-level histogram over the top 12 bits of the total-order key
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
-  __shared__ unsigned long long srt_s[kSmemSort];
-  __shared__ uint32_t hist[256];
+  __shared__ unsigned long long cand[kCand];
+  __shared__ uint32_t hist[1 << kHistBits];
   __shared__ int s_count, s_nkeep;
   __shared__ uint32_t s_prefix, s_target;
   __shared__ unsigned long long s_best[32];
@@ -165,15 +166,28 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     stop = (int)kMusicEnd;
   }
   const bool stop_on = stop >= 0 && step >= c.min_tokens;
-  for (int i = tid; i < V; i += nt) {
-    float l = lc[i];
-    if (lu) {
-      const float u = lu[i];
-      l = round_bf16(u + round_bf16(q.scale * round_bf16(l - u)));
-    }
+  auto mix = [&](int i, float l, float u) -> float {
+    if (lu) l = round_bf16(u + round_bf16(q.scale * round_bf16(l - u)));
     const bool in = (i >= w0 && i < w1) || (stop_on && i == stop);
-    S[i] = in ? l : -INFINITY;
+    return in ? l : -INFINITY;
+  };
+  // 16-byte vectors when every row starts 16-byte aligned
+  const bool vec = (V & 3) == 0 && (p.ldl & 3) == 0;
+  if (vec) {
+    const float4* c4 = reinterpret_cast<const float4*>(lc);
+    const float4* u4 = reinterpret_cast<const float4*>(lu);
+    float4* s4 = reinterpret_cast<float4*>(S);
+#pragma unroll 4
+    for (int j = tid; j < V / 4; j += nt) {
+      const float4 a = c4[j];
+      const float4 u = lu ? u4[j] : a;
+      const int i = 4 * j;
+      s4[j] = make_float4(mix(i, a.x, u.x), mix(i + 1, a.y, u.y), mix(i + 2, a.z, u.z), mix(i + 3, a.w, u.w));
+    }
+  } else {
+    for (int i = tid; i < V; i += nt) S[i] = mix(i, lc[i], lu ? lu[i] : 0.f);
   }
+  for (int i = tid; i < (1 << kHistBits); i += nt) hist[i] = 0;
   __syncthreads();
 
   // ---- B: repetition penalty over the last penalty_window ids (sampling.rs:130-144)
@@ -203,18 +217,37 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const bool t0 = c.temperature == 0.f, t1 = c.temperature == 1.f;
   int bad = 0, nfin = 0;
   unsigned long long best = ~0ull;
-  for (int i = tid; i < V; i += nt) {
-    float s = S[i];
+  auto visit = [&](int i, float s) -> float {
     if (isnan(s) || s == INFINITY) bad = 1;
     if (t0) {
       if (isfinite(s)) best = min(best, composite(s, i));
-      continue;
+      return s;
     }
-    if (!t1) {
-      s = cast(s / c.temperature, legacy);
-      S[i] = s;
+    if (!t1) s = cast(s / c.temperature, legacy);
+    if (isfinite(s)) {
+      ++nfin;
+      atomicAdd(&hist[total_key(s) >> (32 - kHistBits)], 1u);
     }
-    nfin += isfinite(s) ? 1 : 0;
+    return s;
+  };
+  const bool rewrite = !t0 && !t1;
+  if (vec) {
+    float4* s4 = reinterpret_cast<float4*>(S);
+#pragma unroll 4
+    for (int j = tid; j < V / 4; j += nt) {
+      float4 v = s4[j];
+      const int i = 4 * j;
+      v.x = visit(i, v.x);
+      v.y = visit(i + 1, v.y);
+      v.z = visit(i + 2, v.z);
+      v.w = visit(i + 3, v.w);
+      if (rewrite) s4[j] = v;
+    }
+  } else {
+    for (int i = tid; i < V; i += nt) {
+      const float s = visit(i, S[i]);
+      if (rewrite) S[i] = s;
+    }
   }
   if (__syncthreads_or(bad)) {
     if (tid == 0) finish(-5, -1);
@@ -243,9 +276,68 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
 
   // ---- D: exact threshold = score at descending rank min(top_k-1, n-1) (select_nth, :168-172)
   const int rank = (int)min((long long)c.top_k - 1, (long long)n_finite - 1);
+  const int iters = (V + nt - 1) / nt;
+  unsigned long long* gbuf = p.sortbuf + (size_t)b * p.sort_cap;
+  // bucket (top kHistBits key bits) holding the rank-th largest score
+  if (tid == 0) {
+    uint32_t cum = 0;
+    int bstar = 0;
+    for (int d = (1 << kHistBits) - 1; d >= 0; --d) {
+      if (cum + hist[d] > (uint32_t)rank) {
+        bstar = d;
+        break;
+      }
+      cum += hist[d];
+    }
+    s_prefix = (uint32_t)bstar;
+    s_target = cum + hist[bstar];  // elements in buckets >= bstar
+    s_count = 0;
+    s_nkeep = 0;
+  }
+  __syncthreads();
+  const uint32_t bstar = s_prefix, ncand = s_target;
+  // buckets of -0.0 / +0.0: IEEE >= and the total order disagree there, take the general path
+  const bool zero_bucket = bstar == (0x7fffffffu >> (32 - kHistBits)) || bstar == (0x80000000u >> (32 - kHistBits));
+  int n;
+  unsigned long long* srt;
+  if (ncand <= (uint32_t)kCand && !zero_bucket) {
+    // ---- E/F (fast): the top buckets hold every element ranked at or above `rank`; sort
+    // them in shared memory and read the threshold off the sorted list. With a nonzero
+    // threshold, IEEE `>=` (retain, :173) equals key order, so the survivors are a prefix.
+    for (int it = 0; it < iters; ++it) {
+      const int i = it * nt + tid;
+      bool keep = false;
+      float s = 0.f;
+      if (i < V) {
+        s = S[i];
+        keep = isfinite(s) && (total_key(s) >> (32 - kHistBits)) >= bstar;
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      int base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (keep) cand[base + __popc(bal & ((1u << lane) - 1))] = composite(s, i);
+    }
+    __syncthreads();
+    int m = 1;
+    while (m < (int)ncand) m <<= 1;
+    for (int i = (int)ncand + tid; i < m; i += nt) cand[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort(cand, m);
+    const uint32_t thr_key = ~(uint32_t)(cand[rank] >> 32);
+    int mine = 0;
+    for (int i = tid; i < (int)ncand; i += nt) mine += (~(uint32_t)(cand[i] >> 32)) >= thr_key ? 1 : 0;
+    atomicAdd(&s_nkeep, mine);
+    __syncthreads();
+    n = s_nkeep;
+    srt = cand;
+  } else {
+    n = -1;
+    srt = nullptr;
+  }
+  if (n < 0) {
   uint32_t prefix = 0, mask = 0;
   uint32_t target = (uint32_t)rank;
-  const int iters = (V + nt - 1) / nt;
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     for (int i = tid; i < 256; i += nt) hist[i] = 0;
@@ -283,7 +375,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const float thr = total_key_to_float(prefix);
 
   // ---- E: survivors: finite and >= threshold (IEEE), as retain() keeps them (:173)
-  unsigned long long* gbuf = p.sortbuf + (size_t)b * p.sort_cap;
   if (tid == 0) s_count = 0;
   __syncthreads();
   for (int it = 0; it < iters; ++it) {
@@ -301,23 +392,23 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     if (keep) gbuf[base + __popc(bal & ((1u << lane) - 1))] = composite(s, i);
   }
   __syncthreads();
-  const int n = s_count;
+  n = s_count;
 
   // ---- F: sort by (score desc, id asc) (:174)
   int m = 1;
   while (m < n) m <<= 1;
-  unsigned long long* srt;
-  if (m <= kSmemSort) {
-    for (int i = tid; i < m; i += nt) srt_s[i] = i < n ? gbuf[i] : ~0ull;
+  if (m <= kCand) {
+    for (int i = tid; i < m; i += nt) cand[i] = i < n ? gbuf[i] : ~0ull;
     __syncthreads();
-    bitonic_sort(srt_s, m);
-    srt = srt_s;
+    bitonic_sort(cand, m);
+    srt = cand;
   } else {
     for (int i = n + tid; i < m; i += nt) gbuf[i] = ~0ull;
     __syncthreads();
     bitonic_sort(gbuf, m);
     srt = gbuf;
   }
+  }  // general path
 
   // ---- G: top-p, normalisation and the exponential race in warp 0 (:175-213)
   if (warp != 0) return;
