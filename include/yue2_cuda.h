@@ -104,6 +104,22 @@ int yue2_cuda_ar_stack(const float* input, float* out, float* shadow, const Yue2
 int yue2_cuda_cached_attention(const float* q, const float* k, const float* v, float* out, size_t keys,
                                size_t heads, size_t kv, size_t dim, size_t cache, size_t layer);
 
+/* No counterpart in the reference. The same single-query GQA decode attention for callers
+ * that cannot allocate device memory -- code running inside a host framework that owns
+ * every allocation (its own memory pool, or a rule against cudaMalloc/cudaFree after
+ * start-up because they synchronise the device) or threads that may not block in the
+ * allocator. The caller passes device buffers: q [heads*dim], k and v row-major
+ * [keys, kv*dim], out [heads*dim], all bf16 bits, 16-byte aligned; `stream` is a
+ * cudaStream_t (NULL for the default stream). No allocation happens: the split-K partials
+ * and merge counters live in a 2 MiB static device array held on every GPU that loads the
+ * library until exit. Sizes whose partials (heads * (dim + 2) * splits * 4 B, up to 32
+ * splits) exceed it are rejected with YUE2_ERR_INVALID. The first call on a device, with
+ * that device current, looks up the array's device address; make it before any stream
+ * capture. All calls share the array: calls whose kernels overlap on the GPU race. Returns
+ * 0 or a negative YUE2_ERR_* code; the work is asynchronous on `stream`. */
+int yue2_attention_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, uint64_t keys,
+                           uint64_t heads, uint64_t kv, uint64_t dim, void* stream);
+
 /* ================================================================== 2. resident fast path */
 
 typedef struct Yue2Model Yue2Model;
