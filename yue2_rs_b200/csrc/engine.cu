@@ -548,6 +548,10 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
   cudaError_t e = launch_embed(s, pdl, m.rows, R, m.embed, H, g.vocab, m.x, m.flags + 0);
   if (e != cudaSuccess) return e;
   const int splits = splits_for(m, R);
+  // Decode steps (head = true) give every row its own cache, so attention itself applies
+  // the QK norm and RoPE and appends the row's K/V; prefill chunks (rows of one cache,
+  // consecutive positions) append all rows first with the separate kernel.
+  const bool fused = head;
   for (int l = 0; l < g.layers; ++l) {
     const LayerW& w = m.layers[l];
     GemvParams p = {};
@@ -583,7 +587,7 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
     rp.layer = l;
     rp.max_pos = m.max_pos;
     rp.error = m.flags + 1;
-    if ((e = launch_rope_append(s, pdl, rp, R)) != cudaSuccess) return e;
+    if (!fused && (e = launch_rope_append(s, pdl, rp, R)) != cudaSuccess) return e;
     AttnParams ap = {};
     ap.rows = m.rows;
     ap.q = m.qrot;
@@ -594,6 +598,14 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
     ap.layer = l;
     ap.splits = splits;
     ap.scale = 1.0f / sqrtf((float)g.dim);
+    ap.fused = fused ? 1 : 0;
+    ap.qkv = m.qkv;
+    ap.q_norm = w.q_norm;
+    ap.k_norm = w.k_norm;
+    ap.cos_tab = m.cos_tab;
+    ap.sin_tab = m.sin_tab;
+    ap.max_pos = m.max_pos;
+    ap.error = m.flags + 1;
     if ((e = launch_attention(s, pdl, ap, R)) != cudaSuccess) return e;
     // o projection + residual
     p = GemvParams{};
@@ -640,7 +652,7 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase) {
-  return 1 + 6 * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1;
+  return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1;
 }
 
 // Runs (and caches as a CUDA graph) the forward step for R rows already in m.rows.

@@ -79,6 +79,13 @@ struct AttnParams {
   Geometry g;
   int layer, splits;
   float scale;
+  // fused QK norm + RoPE + KV append (rows with distinct caches): q comes from qkv, and the
+  // CTA whose split holds the row's position writes that position's K and V first
+  int fused;
+  const uint16_t* qkv;   // [R, (heads + 2 kvh) * dim]
+  const float *q_norm, *k_norm, *cos_tab, *sin_tab;
+  int max_pos;
+  int32_t* error;
 };
 
 struct RopeParams {

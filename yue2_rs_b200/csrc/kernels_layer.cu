@@ -76,11 +76,6 @@ cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const ui
 }
 
 // ------------------------------------------------------------------ GEMV
-// One warp streams one output row (or a gate/up row pair) at a time with 16-byte
-// L1-bypassing loads, double-buffered in registers across (row, batch) so the next
-// batch is in flight while the current one is reduced. Activations sit in shared
-// memory (bf16, or f32 for raw drop-in inputs). The first batch of weights is
-// requested before griddepcontrol.wait, overlapping the previous kernel's tail.
 template <int XM>
 struct XTraits;
 template <>
@@ -141,36 +136,57 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
   const int nb = (K8 + 32 * CH - 1) / (32 * CH);
   const int row_begin = (int)(((long long)p.N * blockIdx.x) / gridDim.x);
   const int row_end = (int)(((long long)p.N * (blockIdx.x + 1)) / gridDim.x);
-  const int first = row_begin + warp;
-  const int nrows_w = first < row_end ? (row_end - first + nwarps - 1) / nwarps : 0;
-  const int T = nrows_w * nb;
+  // The CTA's (row, batch) items are split into equal contiguous shares, one per warp, so
+  // no warp idles while another finishes a row.
+  const int items = (row_end - row_begin) * nb;
+  const int ia = (int)(((long long)items * warp) / nwarps);
+  const int T = (int)(((long long)items * (warp + 1)) / nwarps) - ia;
   uint4* ring = reinterpret_cast<uint4*>(smem_raw);  // [kStages][NP][CH][NT]
   unsigned char* xbase = smem_raw + (size_t)kStages * NP * CH * NT * 16;
+  float* slots = reinterpret_cast<float*>(xbase + (size_t)RM * K * XTraits<XM>::bytes);  // [rows][nb][NP][RM]
 
   auto wrow = [&](int n) -> const uint16_t* {
     const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
     return p.w[s] + (size_t)(n - p.seg_start[s]) * K;
   };
-  auto issue = [&](int t) {
-    if (t < T) {
-      const int n = first + (t / nb) * nwarps, b = t % nb;
-      const uint16_t* w0 = wrow(n);
-      const uint16_t* w1 = PAIR ? p.wpair + (size_t)n * K : nullptr;
-      uint4* st = ring + (size_t)(t % kStages) * NP * CH * NT;
+  // issue stream: (row, batch) of the next batch to request, advanced incrementally
+  int i_cnt = 0, i_b = ia % nb, i_row = row_begin + ia / nb;
+  const uint16_t* i_w0 = T > 0 ? wrow(i_row) : nullptr;
+  const uint16_t* i_w1 = (PAIR && T > 0) ? p.wpair + (size_t)i_row * K : nullptr;
+  auto issue = [&]() {
+    if (i_cnt < T) {
+      uint4* st = ring + (size_t)(i_cnt & (kStages - 1)) * NP * CH * NT + tid;
+      const int base = i_b * CH * 32 + lane;
+      if ((i_b + 1) * CH * 32 <= K8) {
 #pragma unroll
-      for (int c = 0; c < CH; ++c) {
-        const int idx = (b * CH + c) * 32 + lane;
-        if (idx < K8) {
-          cp_async16(st + c * NT + tid, w0 + (size_t)idx * 8);
-          if (PAIR) cp_async16(st + (CH + c) * NT + tid, w1 + (size_t)idx * 8);
+        for (int c = 0; c < CH; ++c) {
+          cp_async16(st + c * NT, i_w0 + (size_t)(base + c * 32) * 8);
+          if (PAIR) cp_async16(st + (CH + c) * NT, i_w1 + (size_t)(base + c * 32) * 8);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+          if (base + c * 32 < K8) {
+            cp_async16(st + c * NT, i_w0 + (size_t)(base + c * 32) * 8);
+            if (PAIR) cp_async16(st + (CH + c) * NT, i_w1 + (size_t)(base + c * 32) * 8);
+          }
+      }
+      if (++i_b == nb) {
+        i_b = 0;
+        ++i_row;
+        if (i_cnt + 1 < T) {
+          i_w0 = wrow(i_row);
+          if (PAIR) i_w1 = p.wpair + (size_t)i_row * K;
         }
       }
     }
+    ++i_cnt;
     cp_async_commit();  // one group per batch, empty past the end, so counts stay aligned
   };
+  static_assert((kStages & (kStages - 1)) == 0, "ring index uses a mask");
 
 #pragma unroll
-  for (int t = 0; t < kStages - 1; ++t) issue(t);
+  for (int t = 0; t < kStages - 1; ++t) issue();
 
   pdl_wait();
   pdl_trigger();
@@ -207,6 +223,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
       for (int i = tid; i < K; i += NT) xs[r * K + i] = f2bf_exact(round_bf16(round_bf16(xr[i] * scale) * p.gamma[i]));
     }
   }
+  const int nrows = row_end - row_begin;
+  for (int i = tid; i < nrows * nb * NP * RM; i += NT) slots[i] = 0.f;
   __syncthreads();
 
   float acc[NP][RM];
@@ -215,33 +233,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
 #pragma unroll
     for (int r = 0; r < RM; ++r) acc[q][r] = 0.f;
 
-  auto finish = [&](int n) {
+  // Lane sums stay in registers while the warp's items stay on one row; at a row boundary
+  // the warp reduces them and lane 0 stores the partial in the slot of the first batch of
+  // that row it covered. Slots are summed in batch order at the end (deterministic).
+  auto flush = [&](int row_local, int b_first) {
 #pragma unroll
     for (int q = 0; q < NP; ++q)
 #pragma unroll
       for (int r = 0; r < RM; ++r) acc[q][r] = warp_sum(acc[q][r]);
     if (lane == 0) {
-      const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
-      const int col = p.col0[s] + (n - p.seg_start[s]);
 #pragma unroll
-      for (int r = 0; r < RM; ++r) {
-        if (r >= p.R) break;
-        if (EPI == kEpiBf16) {
-          p.ob[(size_t)r * p.ldo + col] = f2bf_round(acc[0][r]);
-        } else if (EPI == kEpiResidual) {
-          float* xr = p.of + (size_t)r * p.ldo + col;
-          *xr = round_bf16(*xr + round_bf16(acc[0][r]));
-        } else if (EPI == kEpiSwiGLU) {
-          const float g = round_bf16(acc[0][r]);
-          const float u = round_bf16(acc[NP - 1][r]);
-          const float a = round_bf16(g / (1.0f + det_expf(-g)));
-          p.ob[(size_t)r * p.ldo + col] = f2bf_round(a * u);
-        } else if (EPI == kEpiLogits) {
-          p.of[(size_t)r * p.ldo + col] = round_bf16(acc[0][r]);
-        } else {
-          p.of[(size_t)r * p.ldo + col] = acc[0][r];
-        }
-      }
+      for (int q = 0; q < NP; ++q)
+#pragma unroll
+        for (int r = 0; r < RM; ++r) slots[((row_local * nb + b_first) * NP + q) * RM + r] = acc[q][r];
     }
 #pragma unroll
     for (int q = 0; q < NP; ++q)
@@ -249,36 +253,79 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
       for (int r = 0; r < RM; ++r) acc[q][r] = 0.f;
   };
 
-  for (int t = 0; t < T; ++t) {
-    cp_async_wait<kStages - 2>();  // this thread's batch t has landed
-    const uint4* st = ring + (size_t)(t % kStages) * NP * CH * NT;
-    const int b = t % nb;
+  // compute stream: row and batch of item t, advanced incrementally
+  int c_row = ia / nb, c_b = ia % nb, c_b0 = c_b;
+  auto dots = [&](const uint4* st, int base, bool guard) {
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const int idx = (b * CH + c) * 32 + lane;
-      if (idx < K8) {
-        uint4 w[NP];
+      const int idx = base + c * 32;
+      if (guard && idx >= K8) continue;
+      uint4 w[NP];
 #pragma unroll
-        for (int q = 0; q < NP; ++q) w[q] = st[(q * CH + c) * NT + tid];
+      for (int q = 0; q < NP; ++q) w[q] = st[(q * CH + c) * NT];
 #pragma unroll
-        for (int r = 0; r < RM; ++r) {
-          if (XM == kXF32) {
-            const float4* xs = reinterpret_cast<const float4*>(xbase) + ((size_t)r * K8 + idx) * 2;
-            const float4 a = xs[0], bb = xs[1];
+      for (int r = 0; r < RM; ++r) {
+        if (XM == kXF32) {
+          const float4* xs = reinterpret_cast<const float4*>(xbase) + ((size_t)r * K8 + idx) * 2;
+          const float4 a = xs[0], bb = xs[1];
 #pragma unroll
-            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_f32(w[q], a, bb, acc[q][r]);
-          } else {
-            const uint4 xv = reinterpret_cast<const uint4*>(xbase)[(size_t)r * K8 + idx];
+          for (int q = 0; q < NP; ++q) acc[q][r] = dot8_f32(w[q], a, bb, acc[q][r]);
+        } else {
+          const uint4 xv = reinterpret_cast<const uint4*>(xbase)[(size_t)r * K8 + idx];
 #pragma unroll
-            for (int q = 0; q < NP; ++q) acc[q][r] = dot8_bf(w[q], xv, acc[q][r]);
-          }
+          for (int q = 0; q < NP; ++q) acc[q][r] = dot8_bf(w[q], xv, acc[q][r]);
         }
       }
     }
-    if (b == nb - 1) finish(first + (t / nb) * nwarps);
-    issue(t + kStages - 1);  // refills the slot batch t-1 used
+  };
+  for (int t = 0; t < T; ++t) {
+    cp_async_wait<kStages - 2>();  // this thread's batch t has landed
+    const uint4* st = ring + (size_t)(t & (kStages - 1)) * NP * CH * NT + tid;
+    const int base = c_b * CH * 32 + lane;
+    if ((c_b + 1) * CH * 32 <= K8) dots(st, base, false);
+    else dots(st, base, true);
+    issue();  // refills the slot batch t-1 used
+    if (++c_b == nb) {  // the row ends inside this warp's share
+      flush(c_row, c_b0);
+      c_b = 0;
+      c_b0 = 0;
+      ++c_row;
+    }
   }
+  if (T > 0 && c_b != 0) flush(c_row, c_b0);  // share ended inside a row
   cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- epilogue: one thread per (row, activation row), rounding where Linear::finish does
+  for (int i = tid; i < nrows * RM; i += NT) {
+    const int row_local = i / RM, r = i % RM;
+    if (r >= p.R) continue;
+    float v[NP];
+#pragma unroll
+    for (int q = 0; q < NP; ++q) {
+      float sum = 0.f;
+      for (int b = 0; b < nb; ++b) sum += slots[((row_local * nb + b) * NP + q) * RM + r];
+      v[q] = sum;
+    }
+    const int n = row_begin + row_local;
+    const int sg = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
+    const int col = p.col0[sg] + (n - p.seg_start[sg]);
+    if (EPI == kEpiBf16) {
+      p.ob[(size_t)r * p.ldo + col] = f2bf_round(v[0]);
+    } else if (EPI == kEpiResidual) {
+      float* xr = p.of + (size_t)r * p.ldo + col;
+      *xr = round_bf16(*xr + round_bf16(v[0]));
+    } else if (EPI == kEpiSwiGLU) {
+      const float g = round_bf16(v[0]);
+      const float u = round_bf16(v[NP - 1]);
+      const float a = round_bf16(g / (1.0f + det_expf(-g)));
+      p.ob[(size_t)r * p.ldo + col] = f2bf_round(a * u);
+    } else if (EPI == kEpiLogits) {
+      p.of[(size_t)r * p.ldo + col] = round_bf16(v[0]);
+    } else {
+      p.of[(size_t)r * p.ldo + col] = v[0];
+    }
+  }
 }
 
 size_t gemv_smem_bytes(int xmode, int K, int R) {
@@ -291,7 +338,11 @@ constexpr int kMaxSmem = 227 * 1024 - 1024;  // opt-in limit minus room for stat
 template <int RM, bool PAIR, int XM, int EPI>
 static cudaError_t gemv_go(cudaStream_t s, bool pdl, const GemvParams& p, int grid) {
   const void* fn = (const void*)gemv_kernel<RM, PAIR, XM, EPI>;
-  const size_t smem = (size_t)kStages * 4 * kGemvThreads * 16 + (size_t)RM * p.K * XTraits<XM>::bytes;
+  constexpr int NP = PAIR ? 2 : 1, CH = PAIR ? 2 : 4;
+  const size_t nb = ((size_t)p.K / 8 + 32 * CH - 1) / (32 * CH);
+  const size_t rows_max = ((size_t)p.N + grid - 1) / grid + 1;
+  const size_t smem = (size_t)kStages * 4 * kGemvThreads * 16 + (size_t)RM * p.K * XTraits<XM>::bytes +
+                      rows_max * nb * NP * RM * 4;
   if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(fn, kMaxSmem);
   if (e != cudaSuccess || g_configure_only) return e;
@@ -334,11 +385,38 @@ cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const Gemv
 // ------------------------------------------------------------------ QK norm + RoPE + KV append
 // One warp per (head, row): q heads are normalised (Norm::heads) and rotated, k heads
 // normalised, rotated and written to the row's page at its position, v heads copied.
+// Norm::heads (tensor.rs:1158-1172) then Rotary::apply (model.rs:151-168) of one head
+// by one warp: src is the head's bf16 projection, v a warp-private [D] f32 buffer that
+// receives the rotated, bf16-valued head.
+template <int D>
+Y2_DEV void norm_rope_head(const uint16_t* src, const float* gamma, float eps, const float* ct, const float* st,
+                           float* v) {
+  constexpr int DL = D / 32, HALF = D / 2;
+  const int lane = threadIdx.x & 31;
+  float x[DL];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < DL; ++e) {
+    x[e] = bf2f(src[lane * DL + e]);
+    ss = fmaf(x[e], x[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float scale = round_bf16(1.0f / sqrtf(ss / (float)D + eps));
+#pragma unroll
+  for (int e = 0; e < DL; ++e) v[lane * DL + e] = round_bf16(round_bf16(x[e] * scale) * gamma[lane * DL + e]);
+  __syncwarp();
+  for (int i = lane; i < HALF; i += 32) {
+    const float a = v[i], b = v[i + HALF], c = ct[i], s = st[i];
+    v[i] = round_bf16(round_bf16(a * c) - round_bf16(b * s));
+    v[i + HALF] = round_bf16(round_bf16(b * c) + round_bf16(a * s));
+  }
+  __syncwarp();
+}
+
 template <int D>
 __global__ void __launch_bounds__(32) rope_append_kernel(const RopeParams p) {
   pdl_wait();
   pdl_trigger();
-  constexpr int DL = D / 32, HALF = D / 2;
   __shared__ float v[D];
   const int hix = blockIdx.x, r = blockIdx.y, lane = threadIdx.x;
   const DevRow row = p.rows[r];
@@ -360,28 +438,11 @@ __global__ void __launch_bounds__(32) rope_append_kernel(const RopeParams p) {
     return;
   }
   const bool is_q = hix < g.heads;
-  const float* gamma = is_q ? p.q_norm : p.k_norm;
-  float x[DL];
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < DL; ++e) {
-    x[e] = bf2f(src[lane * DL + e]);
-    ss = fmaf(x[e], x[e], ss);
-  }
-  ss = warp_sum(ss);
-  const float scale = round_bf16(1.0f / sqrtf(ss / (float)D + g.eps));
-#pragma unroll
-  for (int e = 0; e < DL; ++e) v[lane * DL + e] = round_bf16(round_bf16(x[e] * scale) * gamma[lane * DL + e]);
-  __syncwarp();
-  const float* ct = p.cos_tab + (size_t)pos * HALF;
-  const float* st = p.sin_tab + (size_t)pos * HALF;
+  norm_rope_head<D>(src, is_q ? p.q_norm : p.k_norm, g.eps, p.cos_tab + (size_t)pos * (D / 2),
+                    p.sin_tab + (size_t)pos * (D / 2), v);
   uint16_t* dst = is_q ? p.q_out + (size_t)r * g.heads * D + (size_t)hix * D
                        : page + kv_offset(g, p.layer, 0, hix - g.heads) + (size_t)slot * D;
-  for (int i = lane; i < HALF; i += 32) {
-    const float a = v[i], b = v[i + HALF], c = ct[i], s = st[i];
-    dst[i] = f2bf_round(round_bf16(a * c) - round_bf16(b * s));
-    dst[i + HALF] = f2bf_round(round_bf16(b * c) + round_bf16(a * s));
-  }
+  for (int i = lane; i < D; i += 32) dst[i] = f2bf_exact(v[i]);
 }
 
 cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R) {
@@ -416,10 +477,12 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   float* ps = qs + G * D;                                              // [NW][G][32]
   float* wm = ps + NW * G * 32;                                        // [NW][G]
   float* wl = wm + NW * G;                                             // [NW][G]
+  float* wbuf_all = wl + NW * G;                                       // [NW][D] norm/rope scratch
   __shared__ int s_ticket;
 
-  pdl_wait();
-  pdl_trigger();
+  // Row descriptors are final once the preceding kernel has passed its own wait (it
+  // triggers this launch only then), and cache rows below the new position were written
+  // by earlier steps: read both, and start streaming the first tile, before the wait.
   const int split = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const DevRow row = a.rows[r];
@@ -431,25 +494,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   const int nsplit = (ntiles + tps - 1) / tps;
   if (split >= nsplit) return;
   const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
-
-  const uint16_t* qsrc = a.q + (size_t)r * geo.heads * D + (size_t)g * G * D;
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = bf2f(qsrc[i]);
-  __syncthreads();
-
-  float m[G], l[G], acc[G][DL];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
-  }
   uint16_t* kt = ktile + warp * 32 * D;
   uint16_t* vt = vtile + warp * 32 * D;
-  float* pw = ps + warp * G * 32;
   const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
-
-  for (int t = t0 + warp; t < t1; t += NW) {
+  auto stage = [&](int t) {  // cp.async one 32-key tile of K (swizzled) and V
     const int key0 = t << 5;
     const int nk = min(32, keys - key0);
     const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
@@ -463,6 +511,66 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
       }
     }
     cp_async_commit();
+  };
+  // the tile holding the new position is written in this launch (fused) or by the
+  // preceding kernel (prefill rows): it is never fetched before the wait
+  const int first_tile = t0 + warp;
+  const bool early = a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  if (early) stage(first_tile);
+
+  pdl_wait();
+  pdl_trigger();
+
+  if (a.fused) {
+    const int pos = row.pos;
+    if (pos < 0 || pos >= a.max_pos) {
+      if (threadIdx.x == 0) atomicExch(a.error, 1);
+      return;
+    }
+    const int width = (geo.heads + 2 * geo.kvh) * D;
+    const uint16_t* src = a.qkv + (size_t)r * width;
+    const float* ct = a.cos_tab + (size_t)pos * (D / 2);
+    const float* st = a.sin_tab + (size_t)pos * (D / 2);
+    float* wbuf = wbuf_all + warp * D;
+    for (int h = warp; h < G; h += 4) {
+      norm_rope_head<D>(src + (size_t)(g * G + h) * D, a.q_norm, geo.eps, ct, st, wbuf);
+      for (int i = lane; i < D; i += 32) qs[h * D + i] = wbuf[i];
+      __syncwarp();
+    }
+    if (split == nsplit - 1) {  // this CTA's last tile holds `pos`: write its K and V first
+      uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
+      const size_t slot = (size_t)(pos & (kPageTokens - 1)) * D;
+      if (warp == 0) {
+        norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, a.k_norm, geo.eps, ct, st, wbuf);
+        uint16_t* dst = page + kv_offset(geo, a.layer, 0, g) + slot;
+        for (int i = lane; i < D; i += 32) dst[i] = f2bf_exact(wbuf[i]);
+      } else if (warp == 1) {
+        const uint16_t* vs = src + (size_t)(geo.heads + geo.kvh + g) * D;
+        uint16_t* dst = page + kv_offset(geo, a.layer, 1, g) + slot;
+        for (int i = lane; i < D; i += 32) dst[i] = vs[i];
+      }
+      __threadfence();
+    }
+  } else {
+    const uint16_t* qsrc = a.q + (size_t)r * geo.heads * D + (size_t)g * G * D;
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = bf2f(qsrc[i]);
+  }
+  __syncthreads();
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
+  }
+  float* pw = ps + warp * G * 32;
+
+  for (int t = t0 + warp; t < t1; t += NW) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    if (!(early && t == first_tile)) stage(t);
     cp_async_wait<0>();
     __syncwarp();
 
@@ -604,7 +712,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
 
 int attention_smem_bytes(int dim, int groups) {
   const int tiles = 2 * 4 * 32 * dim * 2;
-  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups) * 4;
+  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4;
   const int merge = 4 * groups * dim * 4;
   return (tiles > merge ? tiles : merge) + extra;
 }

@@ -102,13 +102,13 @@ Y2_DEV void bitonic_sort(T* a, int m) {
     }
 }
 
-constexpr int kCand = 2048;  // candidates / survivors sorted in shared memory
+constexpr int kCand = 2048;  // samples, candidates and survivors sorted in shared memory
 constexpr int kSampleThreads = 1024;
-constexpr int kHistBits = 12;  // first-level histogram over the top 12 bits of the total-order key
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
   __shared__ unsigned long long cand[kCand];
-  __shared__ uint32_t hist[1 << kHistBits];
+  __shared__ float es[kCand];
+  __shared__ uint32_t hist[256];
   __shared__ int s_count, s_nkeep;
   __shared__ uint32_t s_prefix, s_target;
   __shared__ unsigned long long s_best[32];
@@ -187,7 +187,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   } else {
     for (int i = tid; i < V; i += nt) S[i] = mix(i, lc[i], lu ? lu[i] : 0.f);
   }
-  for (int i = tid; i < (1 << kHistBits); i += nt) hist[i] = 0;
   __syncthreads();
 
   // ---- B: repetition penalty over the last penalty_window ids (sampling.rs:130-144)
@@ -224,10 +223,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
       return s;
     }
     if (!t1) s = cast(s / c.temperature, legacy);
-    if (isfinite(s)) {
-      ++nfin;
-      atomicAdd(&hist[total_key(s) >> (32 - kHistBits)], 1u);
-    }
+    if (isfinite(s)) ++nfin;
     return s;
   };
   const bool rewrite = !t0 && !t1;
@@ -278,62 +274,78 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const int rank = (int)min((long long)c.top_k - 1, (long long)n_finite - 1);
   const int iters = (V + nt - 1) / nt;
   unsigned long long* gbuf = p.sortbuf + (size_t)b * p.sort_cap;
-  // bucket (top kHistBits key bits) holding the rank-th largest score
-  if (tid == 0) {
-    uint32_t cum = 0;
-    int bstar = 0;
-    for (int d = (1 << kHistBits) - 1; d >= 0; --d) {
-      if (cum + hist[d] > (uint32_t)rank) {
-        bstar = d;
-        break;
-      }
-      cum += hist[d];
+  // Estimate: sort kCand strided samples of the phase window and take the one expected to
+  // leave 3*(rank+1) + 64 elements at or above it; collect every finite element with a key
+  // at least that large. The collection is exact whenever it holds rank+1 or more elements
+  // (they are then exactly the top of the order); otherwise the general path runs.
+  {
+    constexpr int kSamples = 1024;
+    const int span = w1 - w0;
+    for (int j = tid; j < kSamples; j += nt) {
+      const int i = w0 + (int)(((long long)j * span) / kSamples);
+      const float s = S[i];
+      cand[j] = isfinite(s) ? composite(s, i) : ~0ull;
     }
-    s_prefix = (uint32_t)bstar;
-    s_target = cum + hist[bstar];  // elements in buckets >= bstar
-    s_count = 0;
-    s_nkeep = 0;
-  }
-  __syncthreads();
-  const uint32_t bstar = s_prefix, ncand = s_target;
-  // buckets of -0.0 / +0.0: IEEE >= and the total order disagree there, take the general path
-  const bool zero_bucket = bstar == (0x7fffffffu >> (32 - kHistBits)) || bstar == (0x80000000u >> (32 - kHistBits));
-  int n;
-  unsigned long long* srt;
-  if (ncand <= (uint32_t)kCand && !zero_bucket) {
-    // ---- E/F (fast): the top buckets hold every element ranked at or above `rank`; sort
-    // them in shared memory and read the threshold off the sorted list. With a nonzero
-    // threshold, IEEE `>=` (retain, :173) equals key order, so the survivors are a prefix.
-    for (int it = 0; it < iters; ++it) {
-      const int i = it * nt + tid;
-      bool keep = false;
-      float s = 0.f;
-      if (i < V) {
-        s = S[i];
-        keep = isfinite(s) && (total_key(s) >> (32 - kHistBits)) >= bstar;
-      }
+    if (tid == 0) {
+      s_count = 0;
+      s_nkeep = 0;
+    }
+    __syncthreads();
+    bitonic_sort(cand, kSamples);
+    const double want = 3.0 * (rank + 1) + 64.0;
+    const int jj = (int)min((double)(kSamples - 1), max(0.0, ceil(want * kSamples / (double)span) - 1.0));
+    const unsigned long long est = cand[jj];
+    const uint32_t tau = est == ~0ull ? 0u : ~(uint32_t)(est >> 32);
+    __syncthreads();  // every thread has read cand[jj] before it is overwritten
+    auto take = [&](bool keep, float s, int i) {
       const unsigned bal = __ballot_sync(0xffffffffu, keep);
       int base = 0;
       if (lane == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
       base = __shfl_sync(0xffffffffu, base, 0);
-      if (keep) cand[base + __popc(bal & ((1u << lane) - 1))] = composite(s, i);
+      const int pos = base + __popc(bal & ((1u << lane) - 1));
+      if (keep && pos < kCand) cand[pos] = composite(s, i);
+    };
+    if (vec) {  // four scores per thread per step, the next float4 requested before this one is used
+      const float4* s4 = reinterpret_cast<const float4*>(S);
+      const int V4 = V / 4, it4 = (V4 + nt - 1) / nt;
+      const float4 none = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      float4 cur = tid < V4 ? s4[tid] : none;
+      for (int it = 0; it < it4; ++it) {
+        const int j = it * nt + tid, jn = j + nt;
+        const float4 nxt = (it + 1 < it4 && jn < V4) ? s4[jn] : none;
+        const float e[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) take(isfinite(e[u]) && total_key(e[u]) >= tau, e[u], 4 * j + u);
+        cur = nxt;
+      }
+    } else {
+      for (int it = 0; it < iters; ++it) {
+        const int i = it * nt + tid;
+        const float s = i < V ? S[i] : -INFINITY;
+        take(isfinite(s) && total_key(s) >= tau, s, i);
+      }
     }
     __syncthreads();
+  }
+  const int ncand = s_count;
+  int n = -1;
+  unsigned long long* srt = nullptr;
+  if (ncand > rank && ncand <= kCand) {
     int m = 1;
-    while (m < (int)ncand) m <<= 1;
-    for (int i = (int)ncand + tid; i < m; i += nt) cand[i] = ~0ull;
+    while (m < ncand) m <<= 1;
+    for (int i = ncand + tid; i < m; i += nt) cand[i] = ~0ull;
     __syncthreads();
     bitonic_sort(cand, m);
     const uint32_t thr_key = ~(uint32_t)(cand[rank] >> 32);
-    int mine = 0;
-    for (int i = tid; i < (int)ncand; i += nt) mine += (~(uint32_t)(cand[i] >> 32)) >= thr_key ? 1 : 0;
-    atomicAdd(&s_nkeep, mine);
-    __syncthreads();
-    n = s_nkeep;
-    srt = cand;
-  } else {
-    n = -1;
-    srt = nullptr;
+    // a +-0 threshold: IEEE `>=` (retain, :173) and key order differ there; general path
+    if (thr_key != 0x80000000u && thr_key != 0x7fffffffu) {
+      int mine = 0;
+      for (int i = tid; i < ncand; i += nt) mine += (~(uint32_t)(cand[i] >> 32)) >= thr_key ? 1 : 0;
+      atomicAdd(&s_nkeep, mine);
+      __syncthreads();
+      n = s_nkeep;
+      srt = cand;
+    }
   }
   if (n < 0) {
   uint32_t prefix = 0, mask = 0;
@@ -412,10 +424,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
 
   // ---- G: top-p, normalisation and the exponential race in warp 0 (:175-213)
   if (warp != 0) return;
-  float* E = p.expv + (size_t)b * V;
+  float* E = n <= kCand ? es : p.expv + (size_t)b * V;  // shared memory unless the support is huge
   auto idof = [&](int i) { return (int)(srt[i] & 0xffffffffu); };
-  const float mx = S[idof(0)];
-  for (int i = lane; i < n; i += 32) E[i] = det_expf(S[idof(i)] - mx);
+  auto scoreof = [&](int i) { return total_key_to_float(~(uint32_t)(srt[i] >> 32)); };  // exact inverse
+  const float mx = scoreof(0);
+  for (int i = lane; i < n; i += 32) E[i] = det_expf(scoreof(i) - mx);
   __syncwarp();
   int nkeep = n;
   if (c.top_p < 1.f) {
