@@ -480,8 +480,9 @@ int yue2_cache_read(const Yue2Cache* c, uint64_t layer, uint64_t begin, uint64_t
 // ---------------------------------------------------------------- step encoding
 namespace y2 {
 
+// Splits per (row, kv head): as many as fill one wave of attention CTAs (two per SM).
 int splits_for(const Yue2Model& m, int R) {
-  const int want = (2 * m.sms + m.g.kvh * R - 1) / (m.g.kvh * R);
+  const int want = (2 * m.sms) / (m.g.kvh * R);
   return std::max(1, std::min(m.max_splits, want));
 }
 
@@ -528,6 +529,7 @@ cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R
     if (e != cudaSuccess) return e;
   }
   GemvParams p = {};
+  p.error = m.flags + 2;
   head_params(m, phase, p);
   p.K = m.g.hidden;
   p.R = R;
@@ -555,6 +557,7 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
   for (int l = 0; l < g.layers; ++l) {
     const LayerW& w = m.layers[l];
     GemvParams p = {};
+    p.error = m.flags + 2;
     // fused q|k|v projection with the input RMSNorm in the prologue
     p.w[0] = w.q;
     p.w[1] = w.k;
@@ -693,14 +696,15 @@ int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows) {
   return 0;
 }
 
-// Reads and clears the device error flags (embed token range, RoPE range).
+// Reads and clears the device error flags (embed token range, RoPE range, stream stall).
 int take_flags(Yue2Model& m) {
-  CK(cudaMemcpyAsync(m.pinned_flags, m.flags, 8, cudaMemcpyDeviceToHost, m.stream));
+  CK(cudaMemcpyAsync(m.pinned_flags, m.flags, 12, cudaMemcpyDeviceToHost, m.stream));
   CK(cudaStreamSynchronize(m.stream));
-  const int32_t tok = m.pinned_flags[0], pos = m.pinned_flags[1];
-  if (tok || pos) {
-    CK(cudaMemsetAsync(m.flags, 0, 8, m.stream));
+  const int32_t tok = m.pinned_flags[0], pos = m.pinned_flags[1], stall = m.pinned_flags[2];
+  if (tok || pos || stall) {
+    CK(cudaMemsetAsync(m.flags, 0, 12, m.stream));
     CK(cudaStreamSynchronize(m.stream));
+    if (stall) return fail(YUE2_ERR_TIMEOUT, "a bounded weight-stream wait gave up");
     if (tok) return fail(YUE2_ERR_TOKEN, "Token outside model vocabulary");
     return fail(YUE2_ERR_CAPACITY, "position outside the RoPE table");
   }
@@ -827,6 +831,7 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
   auto one = [&](int layer) -> cudaError_t {
     const LayerW& w = m->layers[layer];
     GemvParams p = {};
+    p.error = m->flags + 2;
     p.R = rows;
     p.eps = g.eps;
     switch (kind) {

@@ -64,7 +64,7 @@ struct Yue2Model {
   float* part = nullptr;
   int32_t* counters = nullptr;
   y2::DevRow* rows = nullptr;
-  int32_t* flags = nullptr;  // [0] token out of range, [1] position outside RoPE table
+  int32_t* flags = nullptr;  // [0] token out of range, [1] position outside RoPE table, [2] GEMV stream stall
   int max_splits = 64;
   static constexpr int kRowSlots = 32;  // pinned staging ring for row descriptors
   y2::DevRow* pinned_rows = nullptr;

@@ -68,6 +68,8 @@ struct GemvParams {
   float* of;             // f32 outputs [R, ldo] (logits / raw) or residual [R, N]
   int ldo;
   const int32_t* skip;   // optional: the whole launch is skipped when *skip != 0
+  int32_t* error;        // optional: set to 1 when a bounded pipeline wait gives up
+  int stages;            // set by the launcher: shared-memory ring depth of the streamed path
 };
 
 struct AttnParams {
@@ -147,6 +149,10 @@ struct SampleParams {
 cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const uint16_t* embed, int hidden,
                          int vocab, float* x, int32_t* error);
 cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid);
+// streamed tensor-core GEMV (one CTA per SM); used by launch_gemv where eligible
+bool gemv_tc_eligible(int xmode, int epi, const GemvParams& p);
+cudaError_t launch_gemv_tc(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, bool configure_only);
+cudaError_t launch_with(cudaStream_t s, bool pdl, dim3 grid, dim3 block, size_t smem, const void* fn, void** args);
 cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R);
 cudaError_t launch_attention(cudaStream_t s, bool pdl, const AttnParams& p, int R);
 cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R);

@@ -359,8 +359,7 @@ static cudaError_t gemv_rows(cudaStream_t s, bool pdl, const GemvParams& p, int 
   return gemv_go<8, PAIR, XM, EPI>(s, pdl, p, grid);
 }
 
-cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
-  if (p.R < 1 || p.R > kMaxRows || (p.K & 7) || p.N < 1) return cudaErrorInvalidValue;
+static cudaError_t launch_gemv_simt(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
   switch (epi) {
     case kEpiBf16:
       if (xmode == kXNorm) return gemv_rows<false, kXNorm, kEpiBf16>(s, pdl, p, grid);
@@ -380,6 +379,21 @@ cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const Gemv
       break;
   }
   return cudaErrorInvalidValue;
+}
+
+// The streamed tensor-core kernel takes every shape it supports (bf16 activations,
+// K % 32 == 0, R <= 8); the SIMT kernel takes the rest (f32 drop-in inputs, odd K).
+// Configuration passes set up both, so either can be chosen at launch time.
+cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
+  if (p.R < 1 || p.R > kMaxRows || (p.K & 7) || p.N < 1) return cudaErrorInvalidValue;
+  const bool tc = gemv_tc_eligible(xmode, epi, p);
+  if (g_configure_only) {
+    cudaError_t e = launch_gemv_simt(s, pdl, xmode, epi, p, grid);
+    if (e == cudaSuccess && tc) e = launch_gemv_tc(s, pdl, xmode, epi, p, true);
+    return e;
+  }
+  if (tc) return launch_gemv_tc(s, pdl, xmode, epi, p, false);
+  return launch_gemv_simt(s, pdl, xmode, epi, p, grid);
 }
 
 // ------------------------------------------------------------------ QK norm + RoPE + KV append
@@ -490,7 +504,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   const Geometry& geo = a.g;
   const int keys = row.pos + 1;
   const int ntiles = (keys + 31) >> 5;
-  const int tps = (ntiles + a.splits - 1) / a.splits;
+  // at least one tile per warp: short caches use fewer splits (the rest exit at once)
+  const int tps = max(NW, (ntiles + a.splits - 1) / a.splits);
   const int nsplit = (ntiles + tps - 1) / tps;
   if (split >= nsplit) return;
   const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
@@ -694,16 +709,35 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   __syncthreads();
   if (s_ticket != nsplit - 1) return;
   __threadfence();
+  // split maxima and sums of every head in one round trip, then each thread's outputs
+  float* sm_ml = wacc;  // [G][nsplit][2] (the warp accumulators are no longer needed)
+  for (int i = threadIdx.x; i < G * nsplit; i += blockDim.x) {
+    const int h = i / nsplit, sp = i % nsplit;
+    const float* ph = part + ((size_t)sp * G + h) * (D + 2);
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(ph));
+    sm_ml[2 * i] = ml.x;
+    sm_ml[2 * i + 1] = ml.y;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int h = i / D, d = i % D;
+    const float* mlh = sm_ml + 2 * h * nsplit;
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(part + ((size_t)s * G + h) * (D + 2)));
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mlh[2 * sp]);
     float L = 0.f, O = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float* ph = part + ((size_t)s * G + h) * (D + 2);
-      const float f = __expf(__ldcg(ph) - M);
-      L = fmaf(__ldcg(ph + 1), f, L);
-      O = fmaf(__ldcg(ph + 2 + d), f, O);
+    constexpr int kB = 8;  // partial outputs requested together
+    for (int s0 = 0; s0 < nsplit; s0 += kB) {
+      float o[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b)
+        o[b] = s0 + b < nsplit ? __ldcg(part + ((size_t)(s0 + b) * G + h) * (D + 2) + 2 + d) : 0.f;
+#pragma unroll
+      for (int b = 0; b < kB; ++b)
+        if (s0 + b < nsplit) {
+          const float f = __expf(mlh[2 * (s0 + b)] - M);
+          L = fmaf(mlh[2 * (s0 + b) + 1], f, L);
+          O = fmaf(o[b], f, O);
+        }
     }
     a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
   }
