@@ -76,17 +76,29 @@ def test_teacher_forced_logits_unit_gains(c1u_device, c1u_oracle, c1_prompt):
 
 
 def test_batched_rows_equal_single_rows(c1u_device, c1_prompt):
-    """Rows in one weight pass do not interact: R=3 gives the R=1 logits bit for bit."""
+    """Rows in one weight pass do not interact. Passes of one or two rows share the SIMT
+    GEMV, so R=2 gives the R=1 logits bit for bit; passes of three to eight rows share the
+    tensor-core GEMV, so a row gives the same logits at R=3 and R=8 whatever its
+    companions hold."""
     prompt, teacher = c1_prompt
-    caches = [c1u_device.new_cache(64) for _ in range(3)]
-    singles = [c1u_device.new_cache(64) for _ in range(3)]
+
+    def caches(n, off):
+        cs = [c1u_device.new_cache(64) for _ in range(n)]
+        for i, c in enumerate(cs):
+            j = (i + off) % 3
+            c1u_device.forward(prompt[j * 5: j * 5 + 7], c)
+        return cs
+
+    ids = lambda n, off: [teacher[(i + off) % 3] for i in range(n)]
+    two = c1u_device.forward_rows(caches(2, 0), ids(2, 0))
+    for i in range(2):
+        one = c1u_device.forward([teacher[i]], caches(1, i)[0])
+        assert (two[i].view(np.uint32) == one.view(np.uint32)).all()
+    three = c1u_device.forward_rows(caches(3, 0), ids(3, 0))
+    eight = c1u_device.forward_rows(caches(8, 0), ids(8, 0))
     for i in range(3):
-        c1u_device.forward(prompt[i * 5: i * 5 + 7], caches[i])
-        c1u_device.forward(prompt[i * 5: i * 5 + 7], singles[i])
-    rows = c1u_device.forward_rows(caches, teacher[:3])
-    for i in range(3):
-        one = c1u_device.forward([teacher[i]], singles[i])
-        assert (rows[i].view(np.uint32) == one.view(np.uint32)).all()
+        assert (three[i].view(np.uint32) == eight[i].view(np.uint32)).all()
+        assert (three[i].view(np.uint32) == eight[i + 3].view(np.uint32)).all()
 
 
 def test_capacity_and_token_errors(c1_device):

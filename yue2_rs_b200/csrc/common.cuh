@@ -72,6 +72,129 @@ Y2_DEV float warp_max(float v) {
   return v;
 }
 
+// ---- activation staging for the GEMVs. Weight copies queued ahead of these loads make
+// every round trip to memory long, so all loads of a batch are issued before any is used.
+
+// Rows [0, R) of a bf16 [R, K] matrix into shared memory rows of `pitch` bytes (K % 8 == 0).
+template <int NT>
+Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs, size_t pitch) {
+  constexpr int kB = 8;
+  const int K8 = K >> 3, total = R * K8, tid = threadIdx.x;
+  for (int base = 0; base < total; base += NT * kB) {
+    uint4 v[kB];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = base + b * NT + tid;
+      if (i < total) v[b] = ldg16(xb + (size_t)i * 8);
+    }
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int i = base + b * NT + tid;
+      if (i < total) {
+        const int r = i / K8, c = i - r * K8;
+        *reinterpret_cast<uint4*>(xs + (size_t)r * pitch + c * 16) = v[b];
+      }
+    }
+  }
+}
+
+// Norm::apply (src/tensor.rs:1140-1157) of rows [0, R) of the f32 residual [R, K] with gains
+// gamma, as bf16 into shared memory rows of `pitch` bytes: s = bf16(1/sqrt(sum x^2 / K + eps)),
+// y = bf16(bf16(x * s) * gamma). K % 4 == 0. Two rows per pass: gains and both rows in one
+// round trip, one block reduction for both. `red` holds 32 floats. Every thread of the
+// block (NT threads, at most 16 warps) takes part.
+template <int NT>
+Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R, float eps, unsigned char* xs,
+                               size_t pitch, float* red) {
+  static_assert(NT % 32 == 0 && NT <= 512, "block size");
+  constexpr int NW = NT / 32;
+  constexpr int kQ = 4;  // float4 columns per thread held in registers
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K4 = K >> 2;
+  const float4* gm = reinterpret_cast<const float4*>(gamma);
+  auto put = [&](int r, int i, const float4& v, const float4& gg, float scale) {
+    const uint32_t a = f2bf_exact(round_bf16(round_bf16(v.x * scale) * gg.x));
+    const uint32_t b = f2bf_exact(round_bf16(round_bf16(v.y * scale) * gg.y));
+    const uint32_t c = f2bf_exact(round_bf16(round_bf16(v.z * scale) * gg.z));
+    const uint32_t d = f2bf_exact(round_bf16(round_bf16(v.w * scale) * gg.w));
+    reinterpret_cast<uint2*>(xs + (size_t)r * pitch)[i] = make_uint2(a | (b << 16), c | (d << 16));
+  };
+  auto sq = [](const float4& v, float s) {
+    s = fmaf(v.x, v.x, s);
+    s = fmaf(v.y, v.y, s);
+    s = fmaf(v.z, v.z, s);
+    return fmaf(v.w, v.w, s);
+  };
+  auto reduce2 = [&](float s0, float s1, int pass, float& t0, float& t1) {
+    s0 = warp_sum(s0);
+    s1 = warp_sum(s1);
+    float* rn = red + (pass & 1) * 16;  // double-buffered: no barrier after the read
+    if (NW <= 8) {
+      if (lane == 0) {
+        rn[warp] = s0;
+        rn[8 + warp] = s1;
+      }
+    }
+    __syncthreads();
+    t0 = 0.f;
+    t1 = 0.f;
+    for (int w = 0; w < NW && w < 8; ++w) {
+      t0 += rn[w];
+      t1 += rn[8 + w];
+    }
+  };
+  if (NW <= 8 && K4 <= kQ * NT) {
+    float4 gv[kQ];
+#pragma unroll
+    for (int q = 0; q < kQ; ++q)
+      if (tid + q * NT < K4) gv[q] = gm[tid + q * NT];
+    for (int r0 = 0, pass = 0; r0 < R; r0 += 2, ++pass) {
+      const bool two = r0 + 1 < R;
+      const float4* x0 = reinterpret_cast<const float4*>(xf + (size_t)r0 * K);
+      const float4* x1 = reinterpret_cast<const float4*>(xf + (size_t)(two ? r0 + 1 : r0) * K);
+      float4 v0[kQ], v1[kQ];
+#pragma unroll
+      for (int q = 0; q < kQ; ++q)
+        if (tid + q * NT < K4) {
+          v0[q] = x0[tid + q * NT];
+          v1[q] = x1[tid + q * NT];
+        }
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int q = 0; q < kQ; ++q)
+        if (tid + q * NT < K4) {
+          s0 = sq(v0[q], s0);
+          s1 = sq(v1[q], s1);
+        }
+      float t0, t1;
+      reduce2(s0, s1, pass, t0, t1);
+      const float sc0 = round_bf16(1.0f / sqrtf(t0 / (float)K + eps));
+      const float sc1 = round_bf16(1.0f / sqrtf(t1 / (float)K + eps));
+#pragma unroll
+      for (int q = 0; q < kQ; ++q)
+        if (tid + q * NT < K4) {
+          put(r0, tid + q * NT, v0[q], gv[q], sc0);
+          if (two) put(r0 + 1, tid + q * NT, v1[q], gv[q], sc1);
+        }
+    }
+  } else {
+    for (int r = 0; r < R; ++r) {
+      const float4* xr = reinterpret_cast<const float4*>(xf + (size_t)r * K);
+      float ss = 0.f;
+      for (int i = tid; i < K4; i += NT) ss = sq(xr[i], ss);
+      ss = warp_sum(ss);
+      __syncthreads();
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float t = 0.f;
+      for (int w = 0; w < NW; ++w) t += red[w];
+      __syncthreads();
+      const float scale = round_bf16(1.0f / sqrtf(t / (float)K + eps));
+      for (int i = tid; i < K4; i += NT) put(r, i, xr[i], gm[i], scale);
+    }
+  }
+}
+
 // dot of 8 bf16 weights with 8 bf16 activations, accumulated into acc
 Y2_DEV float dot8_bf(uint4 w, uint4 x, float acc) {
   acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);

@@ -49,17 +49,6 @@ __host__ __device__ constexpr int piece_bytes(int warps) { return warps * 2 * 32
 // activation rows x four 16-byte pieces) hit distinct banks.
 __host__ __device__ inline size_t x_pitch(int K) { return ((2 * (size_t)K + 127) / 128) * 128 + 64; }
 
-// Sum over the CTA in a fixed order.
-Y2_DEV float cta_sum(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
 
 template <int W, int BC, int kRing, bool PAIR, int XM, int EPI>
 __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
@@ -68,7 +57,6 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
   __shared__ int s_cut[W], s_ncut;
   constexpr int NT = W * 32;
   constexpr int kBlockCols = BC;
-  static_assert(W <= 8, "two-row norm reduction holds 8 warps per row");
   constexpr int kCh = BC / 32;           // 32-column chunks per item = copies per lane per item
   constexpr int kPPR = BC / 8;           // 16-byte pieces per staged row
   constexpr int kRowPitch = row_pitch(BC), kSlot = slot_bytes(BC);
@@ -145,101 +133,9 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
     return;
   }
 
-  // ---- activations. The weight copies queued ahead make every round trip to memory long,
-  // so all loads of a batch are issued before any is used.
-  if (XM == kXBf16) {
-    constexpr int kXB = 8;
-    const int K8 = K >> 3, total = R * K8;
-    for (int base = 0; base < total; base += NT * kXB) {
-      uint4 v[kXB];
-#pragma unroll
-      for (int b = 0; b < kXB; ++b) {
-        const int i = base + b * NT + tid;
-        if (i < total) v[b] = ldg16(p.xb + (size_t)i * 8);
-      }
-#pragma unroll
-      for (int b = 0; b < kXB; ++b) {
-        const int i = base + b * NT + tid;
-        if (i < total) {
-          const int r = i / K8, c = i - r * K8;
-          *reinterpret_cast<uint4*>(xs + (size_t)r * xp + c * 16) = v[b];
-        }
-      }
-    }
-  } else {  // kXNorm: RMSNorm of the f32 residual, bf16 rounded as Norm::apply does
-    const int K4 = K >> 2;
-    const float4* gm = reinterpret_cast<const float4*>(p.gamma);
-    auto put = [&](int r, int i, const float4& v, const float4& gg, float scale) {
-      const uint32_t a = f2bf_exact(round_bf16(round_bf16(v.x * scale) * gg.x));
-      const uint32_t b = f2bf_exact(round_bf16(round_bf16(v.y * scale) * gg.y));
-      const uint32_t c = f2bf_exact(round_bf16(round_bf16(v.z * scale) * gg.z));
-      const uint32_t d = f2bf_exact(round_bf16(round_bf16(v.w * scale) * gg.w));
-      reinterpret_cast<uint2*>(xs + (size_t)r * xp)[i] = make_uint2(a | (b << 16), c | (d << 16));
-    };
-    auto sq = [](const float4& v, float s) {
-      s = fmaf(v.x, v.x, s);
-      s = fmaf(v.y, v.y, s);
-      s = fmaf(v.z, v.z, s);
-      return fmaf(v.w, v.w, s);
-    };
-    constexpr int kQ = 4;  // float4 columns per thread held in registers (K <= 4 * 4 * NT)
-    if (K4 <= kQ * NT) {
-      // two rows per pass: gamma and both rows in one round trip, one reduction for both
-      float4 gv[kQ];
-#pragma unroll
-      for (int q = 0; q < kQ; ++q)
-        if (tid + q * NT < K4) gv[q] = gm[tid + q * NT];
-      for (int r0 = 0, pass = 0; r0 < R; r0 += 2, ++pass) {
-        const bool two = r0 + 1 < R;
-        const float4* x0 = reinterpret_cast<const float4*>(p.xf + (size_t)r0 * K);
-        const float4* x1 = reinterpret_cast<const float4*>(p.xf + (size_t)(two ? r0 + 1 : r0) * K);
-        float4 v0[kQ], v1[kQ];
-#pragma unroll
-        for (int q = 0; q < kQ; ++q)
-          if (tid + q * NT < K4) {
-            v0[q] = x0[tid + q * NT];
-            v1[q] = x1[tid + q * NT];
-          }
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int q = 0; q < kQ; ++q)
-          if (tid + q * NT < K4) {
-            s0 = sq(v0[q], s0);
-            s1 = sq(v1[q], s1);
-          }
-        s0 = warp_sum(s0);
-        s1 = warp_sum(s1);
-        float* rn = red_norm + (pass & 1) * 16;  // double-buffered: no barrier after the read
-        if (lane == 0) {
-          rn[warp] = s0;
-          rn[8 + warp] = s1;
-        }
-        __syncthreads();
-        float t0 = 0.f, t1 = 0.f;
-        for (int w = 0; w < W; ++w) {
-          t0 += rn[w];
-          t1 += rn[8 + w];
-        }
-        const float sc0 = round_bf16(1.0f / sqrtf(t0 / (float)K + p.eps));
-        const float sc1 = round_bf16(1.0f / sqrtf(t1 / (float)K + p.eps));
-#pragma unroll
-        for (int q = 0; q < kQ; ++q)
-          if (tid + q * NT < K4) {
-            put(r0, tid + q * NT, v0[q], gv[q], sc0);
-            if (two) put(r0 + 1, tid + q * NT, v1[q], gv[q], sc1);
-          }
-      }
-    } else {
-      for (int r = 0; r < R; ++r) {
-        const float4* xr = reinterpret_cast<const float4*>(p.xf + (size_t)r * K);
-        float ss = 0.f;
-        for (int i = tid; i < K4; i += NT) ss = sq(xr[i], ss);
-        ss = cta_sum(ss, red_norm);
-        const float scale = round_bf16(1.0f / sqrtf(ss / (float)K + p.eps));
-        for (int i = tid; i < K4; i += NT) put(r, i, xr[i], gm[i], scale);
-      }
-    }
-  }
+  // ---- activations
+  if (XM == kXBf16) stage_bf16_rows<NT>(p.xb, K, R, xs, xp);
+  else stage_rmsnorm_rows<NT>(p.xf, p.gamma, K, R, p.eps, xs, xp, red_norm);
   __syncthreads();
 
   // output of (activation row r, tile row j) of `tile` with value v (SwiGLU: gate v, up u)
@@ -384,10 +280,11 @@ static cudaError_t set_smem_once(const void* fn) {
   return cudaSuccess;
 }
 
-// Path choice: the tensor-core kernel for R > 2 (prefill chunks, batched songs), where the
-// SIMT kernel becomes instruction bound; the SIMT kernel for R <= 2 (one song with CFG),
-// where its two CTAs per SM overlap the neighbouring launches better. YUE2_CUDA_GEMV=tc or
-// =simt forces one path for every shape (measurements).
+// Path choice: the SIMT kernel for R <= 2 (one song with CFG: measured faster in the
+// chained decode step, where its two CTAs per SM overlap the neighbouring launches), the
+// tensor-core kernel for R > 2 (prefill chunks, batched songs), where the SIMT kernel is
+// instruction bound. Within a path a row's result does not depend on the other rows.
+// YUE2_CUDA_GEMV=tc or =simt forces one path for every shape (measurements).
 static int gemv_tc_mode() {
   static const int mode = [] {
     const char* v = getenv("YUE2_CUDA_GEMV");

@@ -103,17 +103,6 @@ Y2_DEV float dot8_f32(uint4 w, const float4& a, const float4& b, float acc) {
   return acc;
 }
 
-// Block-wide f32 sum with a fixed reduction order (identical in every CTA).
-Y2_DEV float block_sum(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
 
 // Weight stream: every thread owns 16-byte chunks of its warp's current row and copies
 // them with cp.async.cg (L2 only) into its own slots of a kStages-deep shared-memory
@@ -202,26 +191,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
       const int r = i / K;
       xs[i] = r < p.R ? p.xf[i] : 0.f;
     }
-  } else if (XM == kXBf16) {
-    uint4* xs = reinterpret_cast<uint4*>(xbase);
-    for (int i = tid; i < RM * K8; i += NT) {
-      const int r = i / K8;
-      xs[i] = r < p.R ? ldg16(p.xb + (size_t)i * 8) : make_uint4(0, 0, 0, 0);
-    }
-  } else {  // kXNorm: RMSNorm of the f32 residual, bf16 rounded as Norm::apply does
-    uint16_t* xs = reinterpret_cast<uint16_t*>(xbase);
-    for (int r = 0; r < RM; ++r) {
-      if (r >= p.R) {
-        for (int i = tid; i < K; i += NT) xs[r * K + i] = 0;
-        continue;
-      }
-      const float* xr = p.xf + (size_t)r * K;
-      float ss = 0.f;
-      for (int i = tid; i < K; i += NT) ss = fmaf(xr[i], xr[i], ss);
-      ss = block_sum(ss, red);
-      const float scale = round_bf16(1.0f / sqrtf(ss / (float)K + p.eps));
-      for (int i = tid; i < K; i += NT) xs[r * K + i] = f2bf_exact(round_bf16(round_bf16(xr[i] * scale) * p.gamma[i]));
-    }
+  } else {
+    // rows past R are zero (the dot loops read all RM rows)
+    uint4* xz = reinterpret_cast<uint4*>(xbase) + (size_t)p.R * K8;
+    for (int i = tid; i < (RM - p.R) * K8; i += NT) xz[i] = make_uint4(0, 0, 0, 0);
+    if (XM == kXBf16) stage_bf16_rows<NT>(p.xb, K, p.R, xbase, (size_t)K * 2);
+    else  // kXNorm: RMSNorm of the f32 residual (Norm::apply)
+      stage_rmsnorm_rows<NT>(p.xf, p.gamma, K, p.R, p.eps, xbase, (size_t)K * 2, red);
   }
   const int nrows = row_end - row_begin;
   for (int i = tid; i < nrows * nb * NP * RM; i += NT) slots[i] = 0.f;
@@ -744,11 +720,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   if (threadIdx.x == 0) a.counters[r * geo.kvh + g] = 0;
 }
 
+// The reservation is at least 77 KB, so that no SM holds more than two attention CTAs: the
+// block scheduler would otherwise stack three on the SMs that free up first and leave
+// others idle.
 int attention_smem_bytes(int dim, int groups) {
   const int tiles = 2 * 4 * 32 * dim * 2;
   const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4;
   const int merge = 4 * groups * dim * 4;
-  return (tiles > merge ? tiles : merge) + extra;
+  const int need = (tiles > merge ? tiles : merge) + extra;
+  return need > 77 * 1024 ? need : 77 * 1024;
 }
 
 template <int D, int G>
