@@ -280,6 +280,33 @@ def main():
                              "hbm_frac_of_measured": sb / (sms / ks * 1e-3) / 1e9 / peak,
                              "hbm_frac_of_8TBs": sb / (sms / ks * 1e-3) / 8e12}
 
+    # ---- config 3 (batched songs): 8 songs of one rank in every weight pass (16 CFG rows) at
+    # a ~1,024-position context (synthetic KV fill ahead of 8-id prompts)
+    batched = {}
+    if not args.no_sweep:
+        B, ks = 8, 24
+        mt = 4 + ks + 1
+        reqs = [Request(cond[8 * i: 8 * i + 8], seed=100 * rank + i, negative=uncond[8 * i: 8 * i + 8], scale=SCALE,
+                        context_fill=PROMPT - 8) for i in range(B)]
+        ss = Session(model, reqs, c2_sampling(mt), Phase.VOCAB)
+        st = torch.cuda.ExternalStream(ss.cuda_stream)
+        ss.step(4)
+        ss.sync()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        ss.step(ks)
+        b.record(st)
+        ss.sync()
+        barrier()
+        bms = max_over_ranks(a.elapsed_time(b))
+        ss.close()
+        ctx = PROMPT + 5 + ks / 2.0
+        sb = weight_bytes(cfg) + 2 * B * kv_bytes_per_token(cfg) * ctx
+        batched = {"songs_per_gpu": B, "rows": 2 * B, "tokens_per_s": world * B * ks / (bms / 1000.0),
+                   "ms_per_step": bms / ks, "context_mid": ctx, "step_bytes": sb,
+                   "hbm_frac_of_measured": sb / (bms / ks * 1e-3) / 1e9 / peak}
+
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()
     t0 = time.perf_counter()
@@ -310,6 +337,7 @@ def main():
                           "frac_of_measured": step_bytes / (ms / K * 1e-3) / 1e9 / peak,
                           "frac_of_8TBs": step_bytes / (ms / K * 1e-3) / 8e12},
         "ctx_sweep": sweep,
+        "batched": batched,
         "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "what": "yue2_generate: 512 tokens per song incl. both 1,024-id prefills, host buffers in/out"},
     }

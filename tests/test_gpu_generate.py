@@ -45,14 +45,63 @@ def test_generate_cfg_matches_replay(c1u_device, c1_prompt, temperature):
     assert g.tokens == want and g.truncated and trunc and len(g.tokens) == 24
 
 
+def replay_batch(model, reqs, s, phase):
+    """The batched decode loop step by step: every row of every song stays in the weight
+    pass until the last song ends (as on the device), so each row goes through the same
+    GEMV path as in generate_batch."""
+    rows, owner = [], []
+    for i, r in enumerate(reqs):
+        rows.append(model.new_cache(len(r.prefix) + s.max_tokens))
+        owner.append((i, 0))
+        if r.scale != 1.0:
+            rows.append(model.new_cache(len(r.negative) + s.max_tokens))
+            owner.append((i, 1))
+    logits = [model.forward_phase(reqs[i].negative if k else reqs[i].prefix, c, phase)
+              for c, (i, k) in zip(rows, owner)]
+    rngs = [OracleRng(r.seed) for r in reqs]
+    toks = [[] for _ in reqs]
+    done = [False] * len(reqs)
+    last = [0] * len(reqs)
+    for step in range(s.max_tokens):
+        for i, r in enumerate(reqs):
+            if done[i]:
+                continue
+            lc = logits[owner.index((i, 0))]
+            mix = cfg_mix(lc, logits[owner.index((i, 1))], r.scale) if r.scale != 1.0 else lc
+            t = ochoose(mix, s, toks[i], step, int(phase), r.legacy, rngs[i])
+            if t == phase.end():
+                done[i] = True
+                continue
+            toks[i].append(t)
+            last[i] = t
+            if step + 1 >= s.max_tokens:
+                done[i] = True
+        if all(done):
+            break
+        out = model.forward_rows(rows, [last[i] for i, _ in owner], phase)
+        logits = [out[j] for j in range(len(rows))]
+    return toks
+
+
 def test_generate_without_cfg_and_batch(c1u_device, c1_prompt):
     p = c1_prompt[0]
     s = Sampling(1.0, 0.9, 40, 1.1, 20, 0, 12)
     reqs = [Request(p[:17], 5), Request(p[30:50], 6, p[60:70], 1.5), Request(p[80:90], 7, p[90:99], 2.0, True)]
     outs = generate_batch(c1u_device, reqs, s, Phase.VOCAB)
-    for r, o in zip(reqs, outs):
-        want, _ = replay(c1u_device, r.prefix, r.negative, r.scale, s, r.seed, Phase.VOCAB, r.legacy)
-        assert o.tokens == want
+    want = replay_batch(c1u_device, reqs, s, Phase.VOCAB)
+    for o, w in zip(outs, want):
+        assert o.tokens == w
+
+
+def test_generate_eight_songs_with_cfg(c1u_device, c1_prompt):
+    """Eight songs with CFG: sixteen rows in every weight pass (the batched configuration)."""
+    p = c1_prompt[0]
+    s = Sampling(1.0, 0.93, 50, 1.1, 20, 0, 10)
+    reqs = [Request(p[10 * i: 10 * i + 12 + i], 40 + i, p[150 + 7 * i: 160 + 7 * i], 1.5) for i in range(8)]
+    outs = generate_batch(c1u_device, reqs, s, Phase.VOCAB)
+    want = replay_batch(c1u_device, reqs, s, Phase.VOCAB)
+    for o, w in zip(outs, want):
+        assert o.tokens == w and len(o.tokens) == 10
 
 
 def test_stop_token_ends_generation():

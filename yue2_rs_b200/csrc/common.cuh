@@ -100,15 +100,16 @@ Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs,
 
 // Norm::apply (src/tensor.rs:1140-1157) of rows [0, R) of the f32 residual [R, K] with gains
 // gamma, as bf16 into shared memory rows of `pitch` bytes: s = bf16(1/sqrt(sum x^2 / K + eps)),
-// y = bf16(bf16(x * s) * gamma). K % 4 == 0. Two rows per pass: gains and both rows in one
-// round trip, one block reduction for both. `red` holds 32 floats. Every thread of the
-// block (NT threads, at most 16 warps) takes part.
+// y = bf16(bf16(x * s) * gamma). K % 4 == 0. Up to four rows per pass: gains and the rows in
+// one round trip, one block reduction for all of them. `red` holds 64 floats. Every thread
+// of the block (NT threads, at most 8 warps for the one-pass form) takes part.
 template <int NT>
 Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R, float eps, unsigned char* xs,
                                size_t pitch, float* red) {
   static_assert(NT % 32 == 0 && NT <= 512, "block size");
   constexpr int NW = NT / 32;
-  constexpr int kQ = 4;  // float4 columns per thread held in registers
+  constexpr int kQ = 4;   // float4 columns per thread held in registers
+  constexpr int kRP = 4;  // rows per pass
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K4 = K >> 2;
   const float4* gm = reinterpret_cast<const float4*>(gamma);
@@ -125,57 +126,41 @@ Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R
     s = fmaf(v.z, v.z, s);
     return fmaf(v.w, v.w, s);
   };
-  auto reduce2 = [&](float s0, float s1, int pass, float& t0, float& t1) {
-    s0 = warp_sum(s0);
-    s1 = warp_sum(s1);
-    float* rn = red + (pass & 1) * 16;  // double-buffered: no barrier after the read
-    if (NW <= 8) {
-      if (lane == 0) {
-        rn[warp] = s0;
-        rn[8 + warp] = s1;
-      }
-    }
-    __syncthreads();
-    t0 = 0.f;
-    t1 = 0.f;
-    for (int w = 0; w < NW && w < 8; ++w) {
-      t0 += rn[w];
-      t1 += rn[8 + w];
-    }
-  };
   if (NW <= 8 && K4 <= kQ * NT) {
     float4 gv[kQ];
 #pragma unroll
     for (int q = 0; q < kQ; ++q)
       if (tid + q * NT < K4) gv[q] = gm[tid + q * NT];
-    for (int r0 = 0, pass = 0; r0 < R; r0 += 2, ++pass) {
-      const bool two = r0 + 1 < R;
-      const float4* x0 = reinterpret_cast<const float4*>(xf + (size_t)r0 * K);
-      const float4* x1 = reinterpret_cast<const float4*>(xf + (size_t)(two ? r0 + 1 : r0) * K);
-      float4 v0[kQ], v1[kQ];
+    for (int r0 = 0, pass = 0; r0 < R; r0 += kRP, ++pass) {
+      float4 v[kRP][kQ];
 #pragma unroll
-      for (int q = 0; q < kQ; ++q)
-        if (tid + q * NT < K4) {
-          v0[q] = x0[tid + q * NT];
-          v1[q] = x1[tid + q * NT];
-        }
-      float s0 = 0.f, s1 = 0.f;
+      for (int k = 0; k < kRP; ++k) {
+        const float4* xr = reinterpret_cast<const float4*>(xf + (size_t)min(r0 + k, R - 1) * K);
 #pragma unroll
-      for (int q = 0; q < kQ; ++q)
-        if (tid + q * NT < K4) {
-          s0 = sq(v0[q], s0);
-          s1 = sq(v1[q], s1);
-        }
-      float t0, t1;
-      reduce2(s0, s1, pass, t0, t1);
-      const float sc0 = round_bf16(1.0f / sqrtf(t0 / (float)K + eps));
-      const float sc1 = round_bf16(1.0f / sqrtf(t1 / (float)K + eps));
+        for (int q = 0; q < kQ; ++q)
+          if (tid + q * NT < K4) v[k][q] = xr[tid + q * NT];
+      }
+      float* rn = red + (pass & 1) * 32;  // double-buffered: no barrier after the read
 #pragma unroll
-      for (int q = 0; q < kQ; ++q)
-        if (tid + q * NT < K4) {
-          put(r0, tid + q * NT, v0[q], gv[q], sc0);
-          if (two) put(r0 + 1, tid + q * NT, v1[q], gv[q], sc1);
-        }
+      for (int k = 0; k < kRP; ++k) {
+        float s = 0.f;
+#pragma unroll
+        for (int q = 0; q < kQ; ++q)
+          if (tid + q * NT < K4) s = sq(v[k][q], s);
+        s = warp_sum(s);
+        if (lane == 0) rn[k * 8 + warp] = s;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kRP; ++k) {
+        if (r0 + k >= R) break;
+        float t = 0.f;
+        for (int w = 0; w < NW; ++w) t += rn[k * 8 + w];
+        const float sc = round_bf16(1.0f / sqrtf(t / (float)K + eps));
+#pragma unroll
+        for (int q = 0; q < kQ; ++q)
+          if (tid + q * NT < K4) put(r0 + k, tid + q * NT, v[k][q], gv[q], sc);
+      }
     }
   } else {
     for (int r = 0; r < R; ++r) {

@@ -749,7 +749,7 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
                  float* logits) {
   if (!m || !caches || !ids) return fail(YUE2_ERR_INVALID, "null argument");
   if (!m->finalized) return fail(YUE2_ERR_INVALID, "model not finalized");
-  if (rows < 1 || rows > (uint64_t)kMaxRows) return fail(YUE2_ERR_INVALID, "rows must be in [1, 8]");
+  if (rows < 1 || rows > (uint64_t)kMaxRows) return fail(YUE2_ERR_INVALID, "rows must be in [1, 16]");
   int rc = check_phase_vocab(*m, phase);
   if (rc) return rc;
   std::set<const Yue2Cache*> seen;

@@ -280,7 +280,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
     R += q.scale != 1.f ? 2 : 1;
   }
   if (R > kMaxRows)
-    return fail(YUE2_ERR_INVALID, "at most 8 decode rows (CFG rows count twice) per session on this path");
+    return fail(YUE2_ERR_INVALID, "at most 16 decode rows (CFG rows count twice) per session");
   if ((rc = y2_set_device(m))) return rc;
   Yue2Session* ss = new Yue2Session();
   ss->m = m;

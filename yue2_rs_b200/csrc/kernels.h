@@ -20,7 +20,7 @@ constexpr int64_t kContext = 24576;
 
 enum Phase { kPhaseAbc = 0, kPhaseSemantic = 1, kPhaseVocab = 2 };
 
-constexpr int kMaxRows = 8;        // rows per weight pass on the CUDA-core GEMV
+constexpr int kMaxRows = 16;       // rows per decode step / prefill chunk (8 songs with CFG)
 constexpr int kPageTokens = 64;    // KV page: 64 positions of every layer
 constexpr int kPageLog2 = 6;
 
@@ -50,7 +50,7 @@ __host__ __device__ inline size_t kv_offset(const Geometry& g, int layer, int kv
 }
 inline size_t page_bytes(const Geometry& g) { return (size_t)g.layers * 2 * g.kvh * kPageTokens * g.dim * 2; }
 
-// ---- GEMV (weight streaming, R <= kMaxRows rows per pass)
+// ---- GEMV (weight streaming; the SIMT kernel takes R <= 8, the tensor-core kernel R <= 16)
 enum XMode { kXBf16 = 0, kXNorm = 1, kXF32 = 2 };
 enum EpiMode { kEpiBf16 = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiLogits = 3, kEpiRawF32 = 4 };
 

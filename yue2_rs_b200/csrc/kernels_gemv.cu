@@ -1,6 +1,6 @@
 // Tensor-core GEMV of the decode step (sm_100a).
 //
-// y[r, n] = sum_k W[n, k] * x[r, k] for R <= 8 activation rows, with the epilogues of
+// y[r, n] = sum_k W[n, k] * x[r, k] for R <= 16 activation rows, with the epilogues of
 // Linear::finish (src/tensor.rs:1102-1118), the residual add (src/tensor.rs:632-640,
 // src/model.rs:586-587), SwiGLU (src/model.rs:206-214) and the bf16 logits of
 // Model::forward_phase (src/model.rs:465-507). The GPU realisation it replaces is
@@ -14,8 +14,8 @@
 // so every request is 256 contiguous bytes. cp.async.wait_group plus __syncwarp is the
 // only wait: no block barrier, no spin, no cross-warp dependency while streaming.
 //
-// Each 16-byte piece is two mma.sync m16n8k16 steps with A = the R activation rows (rows
-// g < R of the fragment) and B = the eight weight rows: the lane's columns 8t..8t+3 act
+// Each 16-byte piece is two mma.sync m16n8k16 steps with A = the R activation rows (the
+// fragment's sixteen rows) and B = the eight weight rows: the lane's columns 8t..8t+3 act
 // as k = {2t, 2t+1, 2t+8, 2t+9} of the first step and 8t+4..8t+7 of the second, and the
 // activations use the same column order, so every dot product is unchanged. Four
 // independent accumulator chains (one per piece) hide the mma latency. A tile that one
@@ -44,7 +44,7 @@ constexpr int kTcMaxSmem = 227 * 1024 - 1024;
 __host__ __device__ constexpr int row_pitch(int bc) { return bc * 2 + 64; }
 __host__ __device__ constexpr int slot_bytes(int bc) { return kTileRows * row_pitch(bc); }
 __host__ __device__ constexpr int ring_bytes(int warps, int bc, int ring) { return warps * ring * slot_bytes(bc); }
-__host__ __device__ constexpr int piece_bytes(int warps) { return warps * 2 * 32 * 8; }
+__host__ __device__ constexpr int piece_bytes(int warps) { return warps * 2 * 32 * 16; }
 // Activation row pitch: 64 mod 128 bytes, so that the eight lanes of a quarter-warp (two
 // activation rows x four 16-byte pieces) hit distinct banks.
 __host__ __device__ inline size_t x_pitch(int K) { return ((2 * (size_t)K + 127) / 128) * 128 + 64; }
@@ -53,7 +53,7 @@ __host__ __device__ inline size_t x_pitch(int K) { return ((2 * (size_t)K + 127)
 template <int W, int BC, int kRing, bool PAIR, int XM, int EPI>
 __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ float red_norm[32];
+  __shared__ float red_norm[64];
   __shared__ int s_cut[W], s_ncut;
   constexpr int NT = W * 32;
   constexpr int kBlockCols = BC;
@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
   const size_t xp = x_pitch(K);
   unsigned char* ring = smem + (size_t)warp * kRing * kSlot;  // [slot][row][kRowPitch]
   unsigned char* xs = smem + ring_bytes(W, BC, kRing);
-  float2* pieces = reinterpret_cast<float2*>(xs + (size_t)R * xp);  // [W][2][32]
+  float4* pieces = reinterpret_cast<float4*>(xs + (size_t)R * xp);  // [W][2][32]
 
   auto wrow = [&](int n) -> const uint16_t* {
     const int s = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
@@ -160,7 +160,8 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
     }
   };
 
-  const bool has_x = g < R;
+  // fragment rows g and g + 8 carry activation rows g and g + 8 (R <= 16)
+  const bool has_x0 = g < R, has_x1 = g + 8 < R;
   const unsigned char* xrow = xs + (size_t)g * xp + t4 * 16;
   constexpr int kAcc = 4;
   float acc[kAcc][4];
@@ -177,36 +178,46 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
 #pragma unroll
     for (int u = 0; u < kCh; ++u) {
       const uint4 w = *reinterpret_cast<const uint4*>(st + u * 64);
-      uint4 x = make_uint4(0u, 0u, 0u, 0u);
-      if (has_x) x = *reinterpret_cast<const uint4*>(xk + u * 64);
-      mma_bf16_16816(acc[u % kAcc], x.x, 0u, x.y, 0u, w.x, w.y);
-      mma_bf16_16816(acc[u % kAcc], x.z, 0u, x.w, 0u, w.z, w.w);
+      uint4 x = make_uint4(0u, 0u, 0u, 0u), y = make_uint4(0u, 0u, 0u, 0u);
+      if (has_x0) x = *reinterpret_cast<const uint4*>(xk + u * 64);
+      if (has_x1) y = *reinterpret_cast<const uint4*>(xk + 8 * xp + u * 64);
+      mma_bf16_16816(acc[u % kAcc], x.x, y.x, x.y, y.y, w.x, w.y);
+      mma_bf16_16816(acc[u % kAcc], x.z, y.z, x.w, y.w, w.z, w.w);
     }
     issue();  // refills the slot item it-1 used
     const bool tile_end = c_kb == nkb - 1;
     if (tile_end || it == T - 1) {
-      float c0 = 0.f, c1 = 0.f;
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) {
         c0 += acc[a][0];
         c1 += acc[a][1];
+        c2 += acc[a][2];
+        c3 += acc[a][3];
         acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
       }
       if (run_kb0 == 0 && tile_end) {
-        // the whole tile is this warp's: lane (g, t) holds rows 2t and 2t+1 of activation g
+        // the whole tile is this warp's: lane (g, t) holds tile rows 2t and 2t+1 of
+        // activations g (c0, c1) and g + 8 (c2, c3)
         if (PAIR) {  // gate rows 0..3 sit in lanes t < 2, up rows 4..7 in lanes t + 2
           const float u0v = __shfl_down_sync(0xffffffffu, c0, 2);
           const float u1v = __shfl_down_sync(0xffffffffu, c1, 2);
+          const float u2v = __shfl_down_sync(0xffffffffu, c2, 2);
+          const float u3v = __shfl_down_sync(0xffffffffu, c3, 2);
           if (t4 < 2) {
             emit(c_tile, g, 2 * t4, c0, u0v);
             emit(c_tile, g, 2 * t4 + 1, c1, u1v);
+            emit(c_tile, g + 8, 2 * t4, c2, u2v);
+            emit(c_tile, g + 8, 2 * t4 + 1, c3, u3v);
           }
         } else {
           emit(c_tile, g, 2 * t4, c0, 0.f);
           emit(c_tile, g, 2 * t4 + 1, c1, 0.f);
+          emit(c_tile, g + 8, 2 * t4, c2, 0.f);
+          emit(c_tile, g + 8, 2 * t4 + 1, c3, 0.f);
         }
       } else {
-        pieces[(warp * 2 + (c_tile == first_tile ? 0 : 1)) * 32 + lane] = make_float2(c0, c1);
+        pieces[(warp * 2 + (c_tile == first_tile ? 0 : 1)) * 32 + lane] = make_float4(c0, c1, c2, c3);
       }
     }
     if (++c_kb == nkb) {
@@ -236,11 +247,12 @@ __global__ void __launch_bounds__(W * 32) gemv_tc_kernel(const GemvParams p) {
     for (int w = 0; w < W; ++w) {
       const int a0 = share(w), a1 = share(w + 1);
       if (a0 >= a1 || a0 >= hi || a1 <= lo) continue;
-      const float2* pw = pieces + (w * 2 + (a0 / nkb == tile ? 0 : 1)) * 32;
-      // element (activation r, tile row q) sits in lane 4r + q/2, component q & 1
+      const float4* pw = pieces + (w * 2 + (a0 / nkb == tile ? 0 : 1)) * 32;
+      // element (activation r, tile row q) sits in lane 4(r % 8) + q/2, component
+      // (q & 1) of (x, y) for r < 8 and of (z, w) for r >= 8
       auto at = [&](int q) {
-        const float2 el = pw[4 * r + (q >> 1)];
-        return (q & 1) ? el.y : el.x;
+        const float4 el = pw[4 * (r & 7) + (q >> 1)];
+        return r < 8 ? ((q & 1) ? el.y : el.x) : ((q & 1) ? el.w : el.z);
       };
       v += at(j);
       if (PAIR) u += at(j + 4);
@@ -299,8 +311,8 @@ static int gemv_tc_mode() {
 struct TcShape {
   int warps, bc, ring, per_sm;
 };
-constexpr TcShape kShapes[] = {{8, 256, 4, 1}, {8, 128, 8, 1}, {4, 256, 4, 2}, {4, 128, 8, 2}, {8, 128, 4, 2},
-                               {8, 128, 4, 1}};
+constexpr TcShape kShapes[] = {{8, 256, 4, 1}, {8, 128, 8, 1}, {8, 128, 4, 1}, {8, 128, 4, 2}, {4, 256, 4, 2},
+                               {4, 128, 8, 2}};
 constexpr int kNumShapes = sizeof(kShapes) / sizeof(kShapes[0]);
 
 static size_t tc_smem(const TcShape& sh, const GemvParams& p) {
@@ -329,7 +341,7 @@ bool gemv_tc_eligible(int xmode, int epi, const GemvParams& p) {
   if (mode == 0 || (mode == 1 && p.R <= 2)) return false;
   if (xmode != kXBf16 && xmode != kXNorm) return false;
   if (epi == kEpiRawF32) return false;
-  if (p.R < 1 || p.R > 8 || p.K < 128 || (p.K % 128) || p.N < 1) return false;
+  if (p.R < 1 || p.R > 16 || p.K < 128 || (p.K % 128) || p.N < 1) return false;
   for (int s = 0; s < 3; ++s)
     if (((uintptr_t)p.w[s]) & 15) return false;
   if (((uintptr_t)p.wpair) & 15) return false;

@@ -116,7 +116,7 @@ constexpr int kStages = 4;
 template <int RM, bool PAIR, int XM, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float red[32];
+  __shared__ float red[64];
   constexpr int NP = PAIR ? 2 : 1;
   constexpr int CH = PAIR ? 2 : 4;  // chunks per lane per batch and matrix
   constexpr int NT = kGemvThreads;
@@ -336,6 +336,7 @@ static cudaError_t gemv_rows(cudaStream_t s, bool pdl, const GemvParams& p, int 
 }
 
 static cudaError_t launch_gemv_simt(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
+  if (p.R > 8) return cudaErrorInvalidValue;
   switch (epi) {
     case kEpiBf16:
       if (xmode == kXNorm) return gemv_rows<false, kXNorm, kEpiBf16>(s, pdl, p, grid);
@@ -357,12 +358,25 @@ static cudaError_t launch_gemv_simt(cudaStream_t s, bool pdl, int xmode, int epi
   return cudaErrorInvalidValue;
 }
 
-// The streamed tensor-core kernel takes every shape it supports (bf16 activations,
-// K % 32 == 0, R <= 8); the SIMT kernel takes the rest (f32 drop-in inputs, odd K).
+// gemv_tc_eligible decides the path (tensor-core kernel: bf16 activations, K % 128 == 0,
+// R <= 16, chosen for R > 2; SIMT kernel: R <= 8, the f32 drop-in input, odd K).
 // Configuration passes set up both, so either can be chosen at launch time.
 cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const GemvParams& p, int grid) {
   if (p.R < 1 || p.R > kMaxRows || (p.K & 7) || p.N < 1) return cudaErrorInvalidValue;
   const bool tc = gemv_tc_eligible(xmode, epi, p);
+  if (p.R > 8 && !tc && !g_configure_only) {
+    // more rows than one pass holds activations for (e.g. 16 rows of an 8,192-column
+    // matrix): two passes over the weights, rows [0, 8) and [8, R)
+    GemvParams a = p, b = p;
+    a.R = 8;
+    b.R = p.R - 8;
+    if (xmode == kXF32 || xmode == kXNorm) b.xf = p.xf + (size_t)8 * p.K;
+    else b.xb = p.xb + (size_t)8 * p.K;
+    if (p.ob) b.ob = p.ob + (size_t)8 * p.ldo;
+    if (p.of) b.of = p.of + (size_t)8 * p.ldo;
+    cudaError_t e = launch_gemv(s, pdl, xmode, epi, a, grid);
+    return e == cudaSuccess ? launch_gemv(s, pdl, xmode, epi, b, grid) : e;
+  }
   if (g_configure_only) {
     cudaError_t e = launch_gemv_simt(s, pdl, xmode, epi, p, grid);
     if (e == cudaSuccess && tc) e = launch_gemv_tc(s, pdl, xmode, epi, p, true);
