@@ -1,0 +1,321 @@
+// Decode attention and the QK norm + RoPE of one head, shared by the standalone kernels
+// (kernels_layer.cu) and the persistent decode-step kernel (kernels_step.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace y2 {
+
+// Norm::heads (tensor.rs:1158-1172) then Rotary::apply (model.rs:151-168) of one head
+// by one warp: src is the head's bf16 projection, v a warp-private [D] f32 buffer that
+// receives the rotated, bf16-valued head.
+template <int D>
+Y2_DEV void norm_rope_head(const uint16_t* src, const float* gamma, float eps, const float* ct, const float* st,
+                           float* v) {
+  constexpr int DL = D / 32, HALF = D / 2;
+  const int lane = threadIdx.x & 31;
+  float x[DL];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < DL; ++e) {
+    x[e] = bf2f(__ldcg(src + lane * DL + e));  // L2: src may come from another SM in this kernel
+    ss = fmaf(x[e], x[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float scale = round_bf16(1.0f / sqrtf(ss / (float)D + eps));
+#pragma unroll
+  for (int e = 0; e < DL; ++e) v[lane * DL + e] = round_bf16(round_bf16(x[e] * scale) * gamma[lane * DL + e]);
+  __syncwarp();
+  for (int i = lane; i < HALF; i += 32) {
+    const float a = v[i], b = v[i + HALF], c = ct[i], s = st[i];
+    v[i] = round_bf16(round_bf16(a * c) - round_bf16(b * s));
+    v[i + HALF] = round_bf16(round_bf16(b * c) + round_bf16(a * s));
+  }
+  __syncwarp();
+}
+
+// Split-K flash decoding. CTA (split, kv head, row) owns a contiguous range of 32-key
+// tiles of the row's cache; each warp stages a tile of K (XOR-swizzled, conflict-free
+// for lane-per-key reads) and V into shared memory with cp.async, computes the G
+// grouped heads' scores with one key per lane, updates an online softmax, and
+// accumulates P.V with lanes over head dims. Warps merge in shared memory; splits
+// merge through f32 partials, and the last split CTA to finish (atomic ticket; no
+// waiting) normalises and writes the bf16 output.
+// 128-thread barrier: the attention body runs on the whole CTA of attn_kernel, or on
+// warps 0-3 of a larger CTA (the persistent step kernel).
+Y2_DEV void attn_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// One (split, kv head, row) item of split-K decode attention on warps 0-3 of the calling
+// CTA. STANDALONE: the attn_kernel launch (programmatic dependent launch, first tile
+// requested before the wait, splits merged by the last CTA through an atomic ticket).
+// Otherwise the caller runs after a grid-wide barrier and merges the partials itself
+// after another one (attn_merge_slice).
+template <int D, int G, bool STANDALONE>
+Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned char* smem_raw) {
+  constexpr int CPR = D / 8;  // 16-byte chunks per key row
+  constexpr int DL = D / 32;  // dims per lane
+  constexpr int NW = 4;
+  uint16_t* ktile = reinterpret_cast<uint16_t*>(smem_raw);           // [NW][32][D]
+  uint16_t* vtile = ktile + NW * 32 * D;                               // [NW][32][D]
+  float* qs = reinterpret_cast<float*>(vtile + NW * 32 * D);           // [G][D]
+  float* ps = qs + G * D;                                              // [NW][G][32]
+  float* wm = ps + NW * G * 32;                                        // [NW][G]
+  float* wl = wm + NW * G;                                             // [NW][G]
+  float* wbuf_all = wl + NW * G;                                       // [NW][D] norm/rope scratch
+  __shared__ int s_ticket;
+
+  // Row descriptors are final once the preceding kernel has passed its own wait (it
+  // triggers this launch only then), and cache rows below the new position were written
+  // by earlier steps: read both, and start streaming the first tile, before the wait.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DevRow row = a.rows[r];
+  if (!row.active) return;
+  const Geometry& geo = a.g;
+  const int keys = row.pos + 1;
+  const int ntiles = (keys + 31) >> 5;
+  // at least one tile per warp: short caches use fewer splits (the rest exit at once)
+  const int tps = max(NW, (ntiles + a.splits - 1) / a.splits);
+  const int nsplit = (ntiles + tps - 1) / tps;
+  if (split >= nsplit) return;
+  const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
+  uint16_t* kt = ktile + warp * 32 * D;
+  uint16_t* vt = vtile + warp * 32 * D;
+  const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
+  auto stage = [&](int t) {  // cp.async one 32-key tile of K (swizzled) and V
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
+    const uint16_t* kb = page + koff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int j = i / CPR, c = i % CPR;
+      if (j < nk) {
+        cp_async16(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
+        cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+      }
+    }
+    cp_async_commit();
+  };
+  // the tile holding the new position is written in this launch (fused) or by the
+  // preceding kernel (prefill rows): it is never fetched before the wait
+  const int first_tile = t0 + warp;
+  const bool early = STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  if (early) stage(first_tile);
+
+  if (STANDALONE) {
+    pdl_wait();
+    pdl_trigger();
+  }
+
+  if (a.fused) {
+    const int pos = row.pos;
+    if (pos < 0 || pos >= a.max_pos) {
+      if (threadIdx.x == 0) atomicExch(a.error, 1);
+      cp_async_wait<0>();
+      return;
+    }
+    const int width = (geo.heads + 2 * geo.kvh) * D;
+    const uint16_t* src = a.qkv + (size_t)r * width;
+    const float* ct = a.cos_tab + (size_t)pos * (D / 2);
+    const float* st = a.sin_tab + (size_t)pos * (D / 2);
+    float* wbuf = wbuf_all + warp * D;
+    for (int h = warp; h < G; h += 4) {
+      norm_rope_head<D>(src + (size_t)(g * G + h) * D, a.q_norm, geo.eps, ct, st, wbuf);
+      for (int i = lane; i < D; i += 32) qs[h * D + i] = wbuf[i];
+      __syncwarp();
+    }
+    if (split == nsplit - 1) {  // this CTA's last tile holds `pos`: write its K and V first
+      uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
+      const size_t slot = (size_t)(pos & (kPageTokens - 1)) * D;
+      if (warp == 0) {
+        norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, a.k_norm, geo.eps, ct, st, wbuf);
+        uint16_t* dst = page + kv_offset(geo, a.layer, 0, g) + slot;
+        for (int i = lane; i < D; i += 32) dst[i] = f2bf_exact(wbuf[i]);
+      } else if (warp == 1) {
+        const uint16_t* vs = src + (size_t)(geo.heads + geo.kvh + g) * D;
+        uint16_t* dst = page + kv_offset(geo, a.layer, 1, g) + slot;
+        for (int i = lane; i < D; i += 32) dst[i] = __ldcg(vs + i);
+      }
+      __threadfence();
+    }
+  } else {
+    const uint16_t* qsrc = a.q + (size_t)r * geo.heads * D + (size_t)g * G * D;
+    for (int i = threadIdx.x; i < G * D; i += 128) qs[i] = bf2f(qsrc[i]);
+  }
+  attn_sync();
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
+  }
+  float* pw = ps + warp * G * 32;
+
+  for (int t = t0 + warp; t < t1; t += NW) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    if (!(early && t == first_tile)) stage(t);
+    cp_async_wait<0>();
+    __syncwarp();
+
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.f;
+    if (lane < nk) {
+#pragma unroll 4
+      for (int c = 0; c < CPR; ++c) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(kt + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
+        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+        const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + c * 8 + 4);
+          float s = sc[h];
+          s = fmaf(qa.x, k0, s);
+          s = fmaf(qa.y, k1, s);
+          s = fmaf(qa.z, k2, s);
+          s = fmaf(qa.w, k3, s);
+          s = fmaf(qb.x, k4, s);
+          s = fmaf(qb.y, k5, s);
+          s = fmaf(qb.z, k6, s);
+          s = fmaf(qb.w, k7, s);
+          sc[h] = s;
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
+      const float mnew = fmaxf(m[h], warp_max(s));
+      const float alpha = m[h] == -INFINITY ? 0.f : __expf(m[h] - mnew);
+      const float pv = lane < nk ? __expf(s - mnew) : 0.f;
+      l[h] = l[h] * alpha + warp_sum(pv);
+      m[h] = mnew;
+      pw[h * 32 + lane] = pv;
+#pragma unroll
+      for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
+    }
+    __syncwarp();
+    for (int j = 0; j < nk; ++j) {
+      const uint16_t* vr = vt + (size_t)j * D + lane * DL;
+      float vv[DL];
+      if constexpr (DL == 2) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
+        vv[0] = bf_lo(w);
+        vv[1] = bf_hi(w);
+      } else if constexpr (DL == 4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(vr);
+        vv[0] = bf_lo(w.x);
+        vv[1] = bf_hi(w.x);
+        vv[2] = bf_lo(w.y);
+        vv[3] = bf_hi(w.y);
+      } else {
+        const uint4 w = *reinterpret_cast<const uint4*>(vr);
+        vv[0] = bf_lo(w.x);
+        vv[1] = bf_hi(w.x);
+        vv[2] = bf_lo(w.y);
+        vv[3] = bf_hi(w.y);
+        vv[4] = bf_lo(w.z);
+        vv[5] = bf_hi(w.z);
+        vv[6] = bf_lo(w.w);
+        vv[7] = bf_hi(w.w);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float pj = pw[h * 32 + j];
+#pragma unroll
+        for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
+  attn_sync();
+  float* wacc = reinterpret_cast<float*>(smem_raw);
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      wm[warp * G + h] = m[h];
+      wl[warp * G + h] = l[h];
+    }
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int e = 0; e < DL; ++e) wacc[((size_t)warp * G + h) * D + lane * DL + e] = acc[h][e];
+  attn_sync();
+
+  const int outw = geo.heads * D;
+  float* part = a.part + ((size_t)(r * geo.kvh + g) * a.splits) * G * (D + 2);
+  for (int i = threadIdx.x; i < G * D; i += 128) {
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * G + h]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float mw = wm[w * G + h];
+      if (mw == -INFINITY) continue;
+      const float f = __expf(mw - M);
+      L = fmaf(wl[w * G + h], f, L);
+      O = fmaf(wacc[((size_t)w * G + h) * D + d], f, O);
+    }
+    if (nsplit == 1) {
+      a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
+    } else {
+      float* ph = part + ((size_t)split * G + h) * (D + 2);
+      if (d == 0) {
+        ph[0] = M;
+        ph[1] = L;
+      }
+      ph[2 + d] = O;
+    }
+  }
+  if (nsplit == 1 || !STANDALONE) return;
+  __threadfence();
+  attn_sync();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(a.counters + r * geo.kvh + g, 1);
+  attn_sync();
+  if (s_ticket != nsplit - 1) return;
+  __threadfence();
+  // split maxima and sums of every head in one round trip, then each thread's outputs
+  float* sm_ml = wacc;  // [G][nsplit][2] (the warp accumulators are no longer needed)
+  for (int i = threadIdx.x; i < G * nsplit; i += 128) {
+    const int h = i / nsplit, sp = i % nsplit;
+    const float* ph = part + ((size_t)sp * G + h) * (D + 2);
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(ph));
+    sm_ml[2 * i] = ml.x;
+    sm_ml[2 * i + 1] = ml.y;
+  }
+  attn_sync();
+  for (int i = threadIdx.x; i < G * D; i += 128) {
+    const int h = i / D, d = i % D;
+    const float* mlh = sm_ml + 2 * h * nsplit;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mlh[2 * sp]);
+    float L = 0.f, O = 0.f;
+    constexpr int kB = 8;  // partial outputs requested together
+    for (int s0 = 0; s0 < nsplit; s0 += kB) {
+      float o[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b)
+        o[b] = s0 + b < nsplit ? __ldcg(part + ((size_t)(s0 + b) * G + h) * (D + 2) + 2 + d) : 0.f;
+#pragma unroll
+      for (int b = 0; b < kB; ++b)
+        if (s0 + b < nsplit) {
+          const float f = __expf(mlh[2 * (s0 + b)] - M);
+          L = fmaf(mlh[2 * (s0 + b) + 1], f, L);
+          O = fmaf(o[b], f, O);
+        }
+    }
+    a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
+  }
+  if (threadIdx.x == 0) a.counters[r * geo.kvh + g] = 0;
+}
+
+}  // namespace y2

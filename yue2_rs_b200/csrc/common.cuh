@@ -76,7 +76,8 @@ Y2_DEV float warp_max(float v) {
 // every round trip to memory long, so all loads of a batch are issued before any is used.
 
 // Rows [0, R) of a bf16 [R, K] matrix into shared memory rows of `pitch` bytes (K % 8 == 0).
-template <int NT>
+// CG: load through L2 only (data written earlier in the same kernel by other SMs).
+template <int NT, bool CG = false>
 Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs, size_t pitch) {
   constexpr int kB = 8;
   const int K8 = K >> 3, total = R * K8, tid = threadIdx.x;
@@ -85,7 +86,7 @@ Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs,
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
       const int i = base + b * NT + tid;
-      if (i < total) v[b] = ldg16(xb + (size_t)i * 8);
+      if (i < total) v[b] = CG ? __ldcg(reinterpret_cast<const uint4*>(xb) + i) : ldg16(xb + (size_t)i * 8);
     }
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
@@ -103,9 +104,10 @@ Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs,
 // y = bf16(bf16(x * s) * gamma). K % 4 == 0. Up to four rows per pass: gains and the rows in
 // one round trip, one block reduction for all of them. `red` holds 64 floats. Every thread
 // of the block (NT threads, at most 8 warps for the one-pass form) takes part.
-template <int NT>
+template <int NT, bool CG = false>
 Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R, float eps, unsigned char* xs,
                                size_t pitch, float* red) {
+  auto ld = [](const float4* p) { return CG ? __ldcg(p) : *p; };
   static_assert(NT % 32 == 0 && NT <= 512, "block size");
   constexpr int NW = NT / 32;
   constexpr int kQ = 4;   // float4 columns per thread held in registers
@@ -138,7 +140,7 @@ Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R
         const float4* xr = reinterpret_cast<const float4*>(xf + (size_t)min(r0 + k, R - 1) * K);
 #pragma unroll
         for (int q = 0; q < kQ; ++q)
-          if (tid + q * NT < K4) v[k][q] = xr[tid + q * NT];
+          if (tid + q * NT < K4) v[k][q] = ld(xr + tid + q * NT);
       }
       float* rn = red + (pass & 1) * 32;  // double-buffered: no barrier after the read
 #pragma unroll
@@ -166,7 +168,7 @@ Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R
     for (int r = 0; r < R; ++r) {
       const float4* xr = reinterpret_cast<const float4*>(xf + (size_t)r * K);
       float ss = 0.f;
-      for (int i = tid; i < K4; i += NT) ss = sq(xr[i], ss);
+      for (int i = tid; i < K4; i += NT) ss = sq(ld(xr + i), ss);
       ss = warp_sum(ss);
       __syncthreads();
       if (lane == 0) red[warp] = ss;
@@ -175,7 +177,7 @@ Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R
       for (int w = 0; w < NW; ++w) t += red[w];
       __syncthreads();
       const float scale = round_bf16(1.0f / sqrtf(t / (float)K + eps));
-      for (int i = tid; i < K4; i += NT) put(r, i, xr[i], gm[i], scale);
+      for (int i = tid; i < K4; i += NT) put(r, i, ld(xr + i), gm[i], scale);
     }
   }
 }

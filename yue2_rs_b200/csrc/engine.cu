@@ -251,6 +251,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   m->gemv_grid = m->sms * std::max(1, env_int("YUE2_CUDA_GEMV_CTAS_PER_SM", 2));
   m->use_pdl = env_int("YUE2_CUDA_PDL", 1) != 0;
   m->use_graphs = env_int("YUE2_CUDA_GRAPHS", 1) != 0;
+  m->use_step = env_int("YUE2_CUDA_STEP", 0) != 0;
   *out = m;
   return 0;
 }
@@ -542,12 +543,218 @@ cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R
   return launch_gemv(s, pdl, kXNorm, kEpiLogits, p, m.gemv_grid);
 }
 
-// embed -> layers -> [final norm + LM head] -> position advance, as one PDL chain.
+// Parameters of layer l's kernels for R rows (shared by the kernel chain and the
+// persistent step kernel's plan).
+struct LayerOps {
+  GemvParams qkv, o, gu, down;
+  RopeParams rope;
+  AttnParams attn;
+};
+
+static LayerOps layer_ops(const Yue2Model& m, int l, int R, bool fused, const int32_t* skip, int splits) {
+  const Geometry& g = m.g;
+  const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
+  const LayerW& w = m.layers[l];
+  LayerOps op;
+  GemvParams p = {};
+  p.error = m.flags + 2;
+  // fused q|k|v projection with the input RMSNorm in the prologue
+  p.w[0] = w.q;
+  p.w[1] = w.k;
+  p.w[2] = w.v;
+  p.seg_start[0] = 0;
+  p.seg_start[1] = qd;
+  p.seg_start[2] = qd + kd;
+  p.col0[0] = 0;
+  p.col0[1] = qd;
+  p.col0[2] = qd + kd;
+  p.N = qd + 2 * kd;
+  p.K = H;
+  p.R = R;
+  p.xf = m.x;
+  p.gamma = w.in_norm;
+  p.eps = g.eps;
+  p.ob = m.qkv;
+  p.ldo = qd + 2 * kd;
+  p.skip = skip;
+  op.qkv = p;
+  RopeParams rp = {};
+  rp.rows = m.rows;
+  rp.qkv = m.qkv;
+  rp.q_out = m.qrot;
+  rp.cos_tab = m.cos_tab;
+  rp.sin_tab = m.sin_tab;
+  rp.q_norm = w.q_norm;
+  rp.k_norm = w.k_norm;
+  rp.g = g;
+  rp.layer = l;
+  rp.max_pos = m.max_pos;
+  rp.error = m.flags + 1;
+  op.rope = rp;
+  AttnParams ap = {};
+  ap.rows = m.rows;
+  ap.q = m.qrot;
+  ap.out = m.attn;
+  ap.part = m.part;
+  ap.counters = m.counters;
+  ap.g = g;
+  ap.layer = l;
+  ap.splits = splits;
+  ap.scale = 1.0f / sqrtf((float)g.dim);
+  ap.fused = fused ? 1 : 0;
+  ap.qkv = m.qkv;
+  ap.q_norm = w.q_norm;
+  ap.k_norm = w.k_norm;
+  ap.cos_tab = m.cos_tab;
+  ap.sin_tab = m.sin_tab;
+  ap.max_pos = m.max_pos;
+  ap.error = m.flags + 1;
+  op.attn = ap;
+  // o projection + residual
+  p = GemvParams{};
+  p.error = m.flags + 2;
+  p.w[0] = p.w[1] = p.w[2] = w.o;
+  p.seg_start[1] = p.seg_start[2] = H;
+  p.N = H;
+  p.K = qd;
+  p.R = R;
+  p.xb = m.attn;
+  p.of = m.x;
+  p.ldo = H;
+  p.skip = skip;
+  op.o = p;
+  // gate|up with the post-attention RMSNorm, SwiGLU epilogue
+  p = GemvParams{};
+  p.error = m.flags + 2;
+  p.w[0] = p.w[1] = p.w[2] = w.gate;
+  p.wpair = w.up;
+  p.seg_start[1] = p.seg_start[2] = I;
+  p.N = I;
+  p.K = H;
+  p.R = R;
+  p.xf = m.x;
+  p.gamma = w.post_norm;
+  p.eps = g.eps;
+  p.ob = m.hbuf;
+  p.ldo = I;
+  p.skip = skip;
+  op.gu = p;
+  // down projection + residual
+  p = GemvParams{};
+  p.error = m.flags + 2;
+  p.w[0] = p.w[1] = p.w[2] = w.down;
+  p.seg_start[1] = p.seg_start[2] = H;
+  p.N = H;
+  p.K = I;
+  p.R = R;
+  p.xb = m.hbuf;
+  p.of = m.x;
+  p.ldo = H;
+  p.skip = skip;
+  op.down = p;
+  return op;
+}
+
+// ---- persistent step kernel: eligibility, plan (device descriptors) and launch
+static bool step_eligible(const Yue2Model& m, int R) {
+  const Geometry& g = m.g;
+  const int G = g.heads / g.kvh;
+  if (!m.use_step || R > 2 || g.dim != 128 || !(G == 1 || G == 2 || G == 3 || G == 4 || G == 8)) return false;
+  const int qd = g.heads * g.dim;
+  if (g.hidden % 256 || g.inter % 256 || qd % 256) return false;
+  const int max_k = std::max(std::max(g.hidden, g.inter), qd);
+  return step_kernel_smem(g.dim, G, R, max_k) <= 227 * 1024 - 1024 - 1024;
+}
+
+static int step_splits(const Yue2Model& m, int R) { return std::max(1, std::min(m.max_splits, m.sms / (m.g.kvh * R))); }
+
+// Builds (once, outside any stream capture) the device descriptors of the step kernel.
+int prepare_step_plan(Yue2Model& m, int R, int phase) {
+  if (!step_eligible(m, R)) return 0;
+  const int key = R * 16 + phase;
+  if (m.step_plans.count(key)) return 0;
+  const Geometry& g = m.g;
+  const int L = g.layers, S = step_splits(m, R);
+  std::vector<StepGemv> ph(4 * L + 1);
+  std::vector<AttnParams> at(L);
+  for (int l = 0; l < L; ++l) {
+    const LayerOps op = layer_ops(m, l, R, true, nullptr, S);
+    ph[4 * l + 0] = StepGemv{op.qkv, kXNorm, kEpiBf16, 0};
+    ph[4 * l + 1] = StepGemv{op.o, kXBf16, kEpiResidual, 0};
+    ph[4 * l + 2] = StepGemv{op.gu, kXNorm, kEpiSwiGLU, 1};
+    ph[4 * l + 3] = StepGemv{op.down, kXBf16, kEpiResidual, 0};
+    at[l] = op.attn;
+  }
+  GemvParams hp = {};
+  hp.error = m.flags + 2;
+  head_params(m, phase, hp);
+  hp.K = g.hidden;
+  hp.R = R;
+  hp.xf = m.x;
+  hp.gamma = m.final_norm;
+  hp.eps = g.eps;
+  hp.of = m.logits;
+  hp.ldo = g.vocab;
+  ph[4 * L] = StepGemv{hp, kXNorm, kEpiLogits, 0};
+  Yue2Model::StepPlan plan;
+  void* p = nullptr;
+  int rc;
+  if ((rc = m.alloc(&p, ph.size() * sizeof(StepGemv)))) return rc;
+  plan.phases = (StepGemv*)p;
+  if ((rc = m.alloc(&p, at.size() * sizeof(AttnParams)))) return rc;
+  plan.attn = (AttnParams*)p;
+  if ((rc = m.alloc(&p, 256))) return rc;
+  plan.barrier = (unsigned*)p;
+  CK(cudaMemcpy(plan.phases, ph.data(), ph.size() * sizeof(StepGemv), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(plan.attn, at.data(), at.size() * sizeof(AttnParams), cudaMemcpyHostToDevice));
+  CK(cudaMemset(plan.barrier, 0, 256));
+  StepParams sp = {};
+  const int G = g.heads / g.kvh;
+  const int max_k = std::max(std::max(g.hidden, g.inter), g.heads * g.dim);
+  sp.smem = step_kernel_smem(g.dim, G, R, max_k);
+  if (launch_step(nullptr, sp, g.dim, G, m.sms, true) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;  // the shape does not fit the kernel: decode keeps the kernel chain
+  }
+  m.step_plans[key] = plan;
+  return 0;
+}
+
+static cudaError_t encode_step(Yue2Model& m, cudaStream_t s, int R, int phase, const int32_t* skip) {
+  const Geometry& g = m.g;
+  const Yue2Model::StepPlan& plan = m.step_plans.at(R * 16 + phase);
+  cudaError_t e;
+  if (phase != kPhaseVocab && (e = launch_fill_f32(s, m.logits, (size_t)R * g.vocab, -INFINITY)) != cudaSuccess)
+    return e;
+  if ((e = cudaMemsetAsync(plan.barrier, 0, 4, s)) != cudaSuccess) return e;
+  StepParams sp = {};
+  sp.phases = plan.phases;
+  sp.attn = plan.attn;
+  sp.layers = g.layers;
+  sp.R = R;
+  sp.rows = m.rows;
+  sp.embed = m.embed;
+  sp.hidden = g.hidden;
+  sp.vocab = g.vocab;
+  sp.x = m.x;
+  sp.tok_error = m.flags + 0;
+  sp.barrier = plan.barrier;
+  sp.stall = m.flags + 2;
+  sp.skip = skip;
+  const int G = g.heads / g.kvh;
+  const int max_k = std::max(std::max(g.hidden, g.inter), g.heads * g.dim);
+  sp.smem = step_kernel_smem(g.dim, G, R, max_k);
+  if ((e = launch_step(s, sp, g.dim, G, m.sms, false)) != cudaSuccess) return e;
+  return launch_step_end(s, m.use_pdl, m.rows, R);
+}
+
+// embed -> layers -> [final norm + LM head] -> position advance, as one PDL chain (or, for
+// decode steps the persistent step kernel covers, one cooperative launch).
 cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip) {
+  if (head && m.step_plans.count(R * 16 + phase)) return encode_step(m, s, R, phase, skip);
   const Geometry& g = m.g;
   const bool pdl = m.use_pdl;
-  const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
-  cudaError_t e = launch_embed(s, pdl, m.rows, R, m.embed, H, g.vocab, m.x, m.flags + 0);
+  cudaError_t e = launch_embed(s, pdl, m.rows, R, m.embed, g.hidden, g.vocab, m.x, m.flags + 0);
   if (e != cudaSuccess) return e;
   const int splits = splits_for(m, R);
   // Decode steps (head = true) give every row its own cache, so attention itself applies
@@ -555,106 +762,20 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
   // consecutive positions) append all rows first with the separate kernel.
   const bool fused = head;
   for (int l = 0; l < g.layers; ++l) {
-    const LayerW& w = m.layers[l];
-    GemvParams p = {};
-    p.error = m.flags + 2;
-    // fused q|k|v projection with the input RMSNorm in the prologue
-    p.w[0] = w.q;
-    p.w[1] = w.k;
-    p.w[2] = w.v;
-    p.seg_start[0] = 0;
-    p.seg_start[1] = qd;
-    p.seg_start[2] = qd + kd;
-    p.col0[0] = 0;
-    p.col0[1] = qd;
-    p.col0[2] = qd + kd;
-    p.N = qd + 2 * kd;
-    p.K = H;
-    p.R = R;
-    p.xf = m.x;
-    p.gamma = w.in_norm;
-    p.eps = g.eps;
-    p.ob = m.qkv;
-    p.ldo = qd + 2 * kd;
-    p.skip = skip;
-    if ((e = launch_gemv(s, pdl, kXNorm, kEpiBf16, p, m.gemv_grid)) != cudaSuccess) return e;
-    RopeParams rp = {};
-    rp.rows = m.rows;
-    rp.qkv = m.qkv;
-    rp.q_out = m.qrot;
-    rp.cos_tab = m.cos_tab;
-    rp.sin_tab = m.sin_tab;
-    rp.q_norm = w.q_norm;
-    rp.k_norm = w.k_norm;
-    rp.g = g;
-    rp.layer = l;
-    rp.max_pos = m.max_pos;
-    rp.error = m.flags + 1;
-    if (!fused && (e = launch_rope_append(s, pdl, rp, R)) != cudaSuccess) return e;
-    AttnParams ap = {};
-    ap.rows = m.rows;
-    ap.q = m.qrot;
-    ap.out = m.attn;
-    ap.part = m.part;
-    ap.counters = m.counters;
-    ap.g = g;
-    ap.layer = l;
-    ap.splits = splits;
-    ap.scale = 1.0f / sqrtf((float)g.dim);
-    ap.fused = fused ? 1 : 0;
-    ap.qkv = m.qkv;
-    ap.q_norm = w.q_norm;
-    ap.k_norm = w.k_norm;
-    ap.cos_tab = m.cos_tab;
-    ap.sin_tab = m.sin_tab;
-    ap.max_pos = m.max_pos;
-    ap.error = m.flags + 1;
-    if ((e = launch_attention(s, pdl, ap, R)) != cudaSuccess) return e;
-    // o projection + residual
-    p = GemvParams{};
-    p.w[0] = p.w[1] = p.w[2] = w.o;
-    p.seg_start[1] = p.seg_start[2] = H;
-    p.N = H;
-    p.K = qd;
-    p.R = R;
-    p.xb = m.attn;
-    p.of = m.x;
-    p.ldo = H;
-    p.skip = skip;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, p, m.gemv_grid)) != cudaSuccess) return e;
-    // gate|up with the post-attention RMSNorm, SwiGLU epilogue
-    p = GemvParams{};
-    p.w[0] = p.w[1] = p.w[2] = w.gate;
-    p.wpair = w.up;
-    p.seg_start[1] = p.seg_start[2] = I;
-    p.N = I;
-    p.K = H;
-    p.R = R;
-    p.xf = m.x;
-    p.gamma = w.post_norm;
-    p.eps = g.eps;
-    p.ob = m.hbuf;
-    p.ldo = I;
-    p.skip = skip;
-    if ((e = launch_gemv(s, pdl, kXNorm, kEpiSwiGLU, p, m.gemv_grid)) != cudaSuccess) return e;
-    // down projection + residual
-    p = GemvParams{};
-    p.w[0] = p.w[1] = p.w[2] = w.down;
-    p.seg_start[1] = p.seg_start[2] = H;
-    p.N = H;
-    p.K = I;
-    p.R = R;
-    p.xb = m.hbuf;
-    p.of = m.x;
-    p.ldo = H;
-    p.skip = skip;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, p, m.gemv_grid)) != cudaSuccess) return e;
+    const LayerOps op = layer_ops(m, l, R, fused, skip, splits);
+    if ((e = launch_gemv(s, pdl, kXNorm, kEpiBf16, op.qkv, m.gemv_grid)) != cudaSuccess) return e;
+    if (!fused && (e = launch_rope_append(s, pdl, op.rope, R)) != cudaSuccess) return e;
+    if ((e = launch_attention(s, pdl, op.attn, R)) != cudaSuccess) return e;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.o, m.gemv_grid)) != cudaSuccess) return e;
+    if ((e = launch_gemv(s, pdl, kXNorm, kEpiSwiGLU, op.gu, m.gemv_grid)) != cudaSuccess) return e;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.down, m.gemv_grid)) != cudaSuccess) return e;
   }
   if (head && (e = encode_head(m, s, pdl, 0, R, 0, phase, skip)) != cudaSuccess) return e;
   return launch_step_end(s, pdl, m.rows, R);
 }
 
-int kernels_per_step(const Yue2Model& m, bool head, int phase) {
+int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
+  if (head && m.step_plans.count(R * 16 + phase)) return 1 + (phase != kPhaseVocab) + 1;
   return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1;
 }
 
@@ -667,6 +788,10 @@ int run_forward(Yue2Model& m, int R, bool head, int phase) {
   }
   auto it = m.graphs.find(key);
   if (it == m.graphs.end()) {
+    if (head) {
+      const int rc = prepare_step_plan(m, R, phase);
+      if (rc) return rc;
+    }
     cudaGraph_t graph;
     CK(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = encode_forward(m, m.stream, R, head, phase, nullptr);

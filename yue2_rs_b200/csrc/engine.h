@@ -41,6 +41,13 @@ struct Yue2Model {
   int sms = 148;
   int gemv_grid = 148;
   bool use_pdl = true, use_graphs = true;
+  bool use_step = false;  // persistent decode-step kernel for R <= 2 (YUE2_CUDA_STEP=1)
+  struct StepPlan {
+    y2::StepGemv* phases = nullptr;
+    y2::AttnParams* attn = nullptr;
+    unsigned* barrier = nullptr;
+  };
+  std::map<int, StepPlan> step_plans;  // key R * 16 + phase
   bool finalized = false, workspace_ready = false;
 
   char* arena = nullptr;
@@ -102,7 +109,8 @@ int check_phase_vocab(const Yue2Model& m, int phase);
 cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip);
 cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R, int dst_row, int phase,
                         const int32_t* skip);
-int kernels_per_step(const Yue2Model& m, bool head, int phase);
+int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
+int prepare_step_plan(Yue2Model& m, int R, int phase);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
 int take_flags(Yue2Model& m);

@@ -391,6 +391,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
 
   // ---- decode step graph: forward(R rows) || MT words, then sample
   if (s->max_tokens > 1) {
+    if ((rc = prepare_step_plan(*m, R, phase))) return bail(rc);
     cudaGraph_t graph;
     if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
       return bail(cuda_fail(e, "capture"));
@@ -425,7 +426,7 @@ void* yue2_session_stream(Yue2Session* ss) { return ss ? (void*)ss->m->stream : 
 
 uint64_t yue2_session_kernels_per_step(const Yue2Session* ss) {
   if (!ss) return 0;
-  return (uint64_t)kernels_per_step(*ss->m, true, ss->phase) + (ss->s.temperature != 0.f ? 1 : 0) + 1;
+  return (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R) + (ss->s.temperature != 0.f ? 1 : 0) + 1;
 }
 
 int yue2_session_step(Yue2Session* ss, uint64_t steps, uint64_t* launched) {
