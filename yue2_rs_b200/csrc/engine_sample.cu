@@ -85,6 +85,7 @@ struct SamplerBufs {
   float *scores = nullptr, *expv = nullptr;
   unsigned long long* sortbuf = nullptr;
   int32_t* flags = nullptr;  // [0] live requests, [1] all done
+  SampleAcc* acc = nullptr;
   int sort_cap = 0;
   std::vector<void*> owned;
 
@@ -107,6 +108,12 @@ struct SamplerBufs {
         (rc = get((void**)&flags, 64)))
       return rc;
     if (need_words && (rc = get((void**)&words, n * 2 * V * 4))) return rc;
+    if ((rc = get((void**)&acc, n * sizeof(SampleAcc)))) return rc;
+    std::vector<SampleAcc> zero(n, SampleAcc{0, 0, ~0ull});
+    if (cudaMemcpy(acc, zero.data(), n * sizeof(SampleAcc), cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(YUE2_ERR_CUDA, "sampler accumulator initialisation failed");
+    }
     return 0;
   }
   ~SamplerBufs() {
@@ -129,6 +136,7 @@ SampleParams make_params(Yue2Model& m, SamplerBufs& b, const SampleCfg& cfg, int
   p.sort_cap = b.sort_cap;
   p.live = b.flags;
   p.all_done = b.flags + 1;
+  p.acc = b.acc;
   return p;
 }
 
@@ -426,7 +434,7 @@ void* yue2_session_stream(Yue2Session* ss) { return ss ? (void*)ss->m->stream : 
 
 uint64_t yue2_session_kernels_per_step(const Yue2Session* ss) {
   if (!ss) return 0;
-  return (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R) + (ss->s.temperature != 0.f ? 1 : 0) + 1;
+  return (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R) + (ss->s.temperature != 0.f ? 1 : 0) + 2;
 }
 
 int yue2_session_step(Yue2Session* ss, uint64_t steps, uint64_t* launched) {

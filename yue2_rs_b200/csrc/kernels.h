@@ -130,6 +130,13 @@ struct MtState {
   uint32_t pad[3];
 };
 
+// Per-request results of the sampler's first passes (sample_prep_kernel), consumed and reset
+// by sample_kernel: any NaN/+inf score, the finite count, the greedy (T=0) argmax key.
+struct SampleAcc {
+  int32_t bad, nfin;
+  unsigned long long best;
+};
+
 struct SampleParams {
   const float* logits;
   int ldl, vocab;
@@ -143,6 +150,7 @@ struct SampleParams {
   int sort_cap;            // power of two >= vocab
   int32_t* live;           // requests not yet done; the last to finish sets *all_done
   int32_t* all_done;
+  SampleAcc* acc;          // [nreq], {0, 0, ~0} between steps
 };
 
 // ---- persistent decode step (kernels_step.cu)

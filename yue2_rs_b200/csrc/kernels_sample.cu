@@ -104,6 +104,129 @@ Y2_DEV void bitonic_sort(T* a, int m) {
 
 constexpr int kCand = 2048;  // samples, candidates and survivors sorted in shared memory
 constexpr int kSampleThreads = 1024;
+constexpr int kPrepChunks = 32;  // CTAs per request in sample_prep_kernel
+constexpr int kPrepThreads = 256;
+
+// Phase window [w0, w1) and stop id of choose (sampling.rs:112-129); stop = -1 for none.
+Y2_DEV void phase_window(int phase, int V, int& w0, int& w1, int& stop) {
+  w0 = 0;
+  w1 = V;
+  stop = -1;
+  if (phase == kPhaseAbc) {
+    w1 = (int)kEOD;
+    stop = (int)kAbcEnd;
+  } else if (phase == kPhaseSemantic) {
+    w0 = (int)kCodecOffset;
+    w1 = (int)(kCodecOffset + kCodecSize);
+    stop = (int)kMusicEnd;
+  }
+}
+
+// The first three passes of choose over one request's vocabulary, split over
+// kPrepChunks CTAs (each a contiguous id range, staged in shared memory):
+// A: CFG mix (sampling.rs:261-266) and phase window (sampling.rs:112-129);
+// B: repetition penalty over the last penalty_window ids (sampling.rs:130-144);
+// C: invalid-logit check, temperature, finite count (sampling.rs:145-167), and for T=0
+//    the argmax key (highest total-order score, lowest id; sampling.rs:148-156).
+// Every element goes through the same operations as in the single-CTA form. The scores
+// go to p.scores; the flag, count and key are combined into p.acc[request] by atomics
+// (order-independent: or, sum, min).
+__global__ void __launch_bounds__(kPrepThreads) sample_prep_kernel(const SampleParams p) {
+  extern __shared__ float sv[];  // this CTA's id range
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, ch = blockIdx.y, tid = threadIdx.x;
+  const SampleReq& q = p.reqs[b];
+  if (q.done) return;
+  const int V = p.vocab;
+  const SampleCfg c = p.cfg;
+  const bool legacy = q.legacy != 0;
+  const int V4 = V >> 2;
+  const bool vec = (V & 3) == 0 && (p.ldl & 3) == 0;
+  // ranges start on multiples of 4 ids when the rows allow 16-byte loads
+  const int lo = vec ? 4 * (int)(((long long)V4 * ch) / kPrepChunks) : (int)(((long long)V * ch) / kPrepChunks);
+  const int hi = vec ? 4 * (int)(((long long)V4 * (ch + 1)) / kPrepChunks)
+                     : (int)(((long long)V * (ch + 1)) / kPrepChunks);
+  const float* lc = p.logits + (size_t)q.cond_row * p.ldl;
+  const float* lu = q.uncond_row >= 0 ? p.logits + (size_t)q.uncond_row * p.ldl : nullptr;
+  const int step = q.step, hlen = q.hist_len;
+  int w0, w1, stop;
+  phase_window(c.phase, V, w0, w1, stop);
+  const bool stop_on = stop >= 0 && step >= c.min_tokens;
+  auto mix = [&](int i, float l, float u) -> float {
+    if (lu) l = round_bf16(u + round_bf16(q.scale * round_bf16(l - u)));
+    const bool in = (i >= w0 && i < w1) || (stop_on && i == stop);
+    return in ? l : -INFINITY;
+  };
+  // ---- A
+  if (vec) {
+    const float4* c4 = reinterpret_cast<const float4*>(lc);
+    const float4* u4 = reinterpret_cast<const float4*>(lu);
+#pragma unroll 4
+    for (int j = lo / 4 + tid; j < hi / 4; j += kPrepThreads) {
+      const float4 a = c4[j];
+      const float4 u = lu ? u4[j] : a;
+      const int i = 4 * j;
+      sv[i - lo] = mix(i, a.x, u.x);
+      sv[i - lo + 1] = mix(i + 1, a.y, u.y);
+      sv[i - lo + 2] = mix(i + 2, a.z, u.z);
+      sv[i - lo + 3] = mix(i + 3, a.w, u.w);
+    }
+  } else {
+    for (int i = lo + tid; i < hi; i += kPrepThreads) sv[i - lo] = mix(i, lc[i], lu ? lu[i] : 0.f);
+  }
+  __syncthreads();
+  // ---- B: ids of this range among the last penalty_window generated ids
+  {
+    const int from = max(0, hlen - c.penalty_window);
+    const int n = hlen - from;
+    for (int k = tid; k < n; k += kPrepThreads) {
+      const int id = q.tokens[from + k];
+      if (id < lo || id >= hi) continue;
+      bool first = true;
+      int cnt = 0;
+      for (int j = 0; j < n; ++j)
+        if (q.tokens[from + j] == id) {
+          if (j < k) first = false;
+          ++cnt;
+        }
+      if (first) {
+        const float alpha = cast(powi_f32(c.repetition_penalty, cnt), legacy);
+        const float s = sv[id - lo];
+        sv[id - lo] = cast(s < 0.f ? s * alpha : s / alpha, legacy);
+      }
+    }
+  }
+  __syncthreads();
+  // ---- C
+  const bool t0 = c.temperature == 0.f, t1 = c.temperature == 1.f;
+  int bad = 0, nfin = 0;
+  unsigned long long best = ~0ull;
+  float* S = p.scores + (size_t)b * V;
+  for (int i = lo + tid; i < hi; i += kPrepThreads) {
+    float s = sv[i - lo];
+    if (isnan(s) || s == INFINITY) bad = 1;
+    if (t0) {
+      if (isfinite(s)) best = min(best, composite(s, i));
+    } else {
+      if (!t1) s = cast(s / c.temperature, legacy);
+      if (isfinite(s)) ++nfin;
+    }
+    S[i] = s;
+  }
+  bad = __syncthreads_or(bad);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nfin += __shfl_xor_sync(0xffffffffu, nfin, o);
+    best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+  }
+  if ((tid & 31) == 0) {
+    SampleAcc& a = p.acc[b];
+    if (nfin) atomicAdd(&a.nfin, nfin);
+    if (best != ~0ull) atomicMin(&a.best, best);
+    if (tid == 0 && bad) atomicOr(&a.bad, 1);
+  }
+}
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
   __shared__ unsigned long long cand[kCand];
@@ -111,7 +234,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   __shared__ uint32_t hist[256];
   __shared__ int s_count, s_nkeep;
   __shared__ uint32_t s_prefix, s_target;
-  __shared__ unsigned long long s_best[32];
   __shared__ float s_sum;
 
   pdl_wait();
@@ -123,8 +245,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const SampleCfg c = p.cfg;
   const bool legacy = q.legacy != 0;
   float* S = p.scores + (size_t)b * V;
-  const float* lc = p.logits + (size_t)q.cond_row * p.ldl;
-  const float* lu = q.uncond_row >= 0 ? p.logits + (size_t)q.uncond_row * p.ldl : nullptr;
   const int step = q.step, hlen = q.hist_len;
 
   auto finish = [&](int status, int id) {  // thread 0 only
@@ -155,116 +275,30 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     }
   };
 
-  // ---- A: CFG mix (sampling.rs:261-266) and phase window (sampling.rs:112-129)
-  int w0 = 0, w1 = V, stop = -1;
-  if (c.phase == kPhaseAbc) {
-    w1 = (int)kEOD;
-    stop = (int)kAbcEnd;
-  } else if (c.phase == kPhaseSemantic) {
-    w0 = (int)kCodecOffset;
-    w1 = (int)(kCodecOffset + kCodecSize);
-    stop = (int)kMusicEnd;
-  }
-  const bool stop_on = stop >= 0 && step >= c.min_tokens;
-  auto mix = [&](int i, float l, float u) -> float {
-    if (lu) l = round_bf16(u + round_bf16(q.scale * round_bf16(l - u)));
-    const bool in = (i >= w0 && i < w1) || (stop_on && i == stop);
-    return in ? l : -INFINITY;
-  };
-  // 16-byte vectors when every row starts 16-byte aligned
-  const bool vec = (V & 3) == 0 && (p.ldl & 3) == 0;
-  if (vec) {
-    const float4* c4 = reinterpret_cast<const float4*>(lc);
-    const float4* u4 = reinterpret_cast<const float4*>(lu);
-    float4* s4 = reinterpret_cast<float4*>(S);
-#pragma unroll 4
-    for (int j = tid; j < V / 4; j += nt) {
-      const float4 a = c4[j];
-      const float4 u = lu ? u4[j] : a;
-      const int i = 4 * j;
-      s4[j] = make_float4(mix(i, a.x, u.x), mix(i + 1, a.y, u.y), mix(i + 2, a.z, u.z), mix(i + 3, a.w, u.w));
-    }
-  } else {
-    for (int i = tid; i < V; i += nt) S[i] = mix(i, lc[i], lu ? lu[i] : 0.f);
+  // ---- A-C ran in sample_prep_kernel: scores in S, flag/count/argmax key in p.acc[b]
+  const bool vec = (V & 3) == 0;  // 16-byte score loads (S rows are V floats apart)
+  int w0, w1, stop;
+  phase_window(c.phase, V, w0, w1, stop);
+  const bool t0 = c.temperature == 0.f;
+  __shared__ SampleAcc s_acc;
+  if (tid == 0) {
+    s_acc = p.acc[b];
+    p.acc[b] = SampleAcc{0, 0, ~0ull};  // ready for the next step's prep
+    s_count = 0;
   }
   __syncthreads();
-
-  // ---- B: repetition penalty over the last penalty_window ids (sampling.rs:130-144)
-  {
-    const int from = max(0, hlen - c.penalty_window);
-    const int n = hlen - from;
-    if (tid < n) {
-      const int id = q.tokens[from + tid];
-      bool first = true;
-      int cnt = 0;
-      for (int j = 0; j < n; ++j)
-        if (q.tokens[from + j] == id) {
-          if (j < tid) first = false;
-          ++cnt;
-        }
-      if (first && id >= 0 && id < V) {
-        const float alpha = cast(powi_f32(c.repetition_penalty, cnt), legacy);
-        const float s = S[id];
-        S[id] = cast(s < 0.f ? s * alpha : s / alpha, legacy);
-      }
-    }
-  }
-  if (tid == 0) s_count = 0;
-  __syncthreads();
-
-  // ---- C: invalid logits, temperature, finite count (sampling.rs:145-167)
-  const bool t0 = c.temperature == 0.f, t1 = c.temperature == 1.f;
-  int bad = 0, nfin = 0;
-  unsigned long long best = ~0ull;
-  auto visit = [&](int i, float s) -> float {
-    if (isnan(s) || s == INFINITY) bad = 1;
-    if (t0) {
-      if (isfinite(s)) best = min(best, composite(s, i));
-      return s;
-    }
-    if (!t1) s = cast(s / c.temperature, legacy);
-    if (isfinite(s)) ++nfin;
-    return s;
-  };
-  const bool rewrite = !t0 && !t1;
-  if (vec) {
-    float4* s4 = reinterpret_cast<float4*>(S);
-#pragma unroll 4
-    for (int j = tid; j < V / 4; j += nt) {
-      float4 v = s4[j];
-      const int i = 4 * j;
-      v.x = visit(i, v.x);
-      v.y = visit(i + 1, v.y);
-      v.z = visit(i + 2, v.z);
-      v.w = visit(i + 3, v.w);
-      if (rewrite) s4[j] = v;
-    }
-  } else {
-    for (int i = tid; i < V; i += nt) {
-      const float s = visit(i, S[i]);
-      if (rewrite) S[i] = s;
-    }
-  }
-  if (__syncthreads_or(bad)) {
+  if (s_acc.bad) {
     if (tid == 0) finish(-5, -1);
     return;
   }
   if (t0) {  // greedy: highest total-order score, lowest id (sampling.rs:148-156)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (lane == 0) s_best[warp] = best;
-    __syncthreads();
     if (tid == 0) {
-      unsigned long long bb = ~0ull;
-      for (int w = 0; w < nt / 32; ++w) bb = min(bb, s_best[w]);
-      if (bb == ~0ull) finish(-6, -1);
-      else finish(0, (int)(bb & 0xffffffffu));
+      if (s_acc.best == ~0ull) finish(-6, -1);
+      else finish(0, (int)(s_acc.best & 0xffffffffu));
     }
     return;
   }
-  atomicAdd(&s_count, nfin);
-  __syncthreads();
-  const int n_finite = s_count;
+  const int n_finite = s_acc.nfin;
   if (n_finite == 0) {
     if (tid == 0) finish(-6, -1);
     return;
@@ -491,18 +525,34 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   if (lane == 0) finish(0, any ? bid : 0);
 }
 
+// Launches the prep passes (kPrepChunks CTAs per request) and then the selection and
+// draw (one CTA per request) as a programmatic-dependent pair.
 cudaError_t launch_sample(cudaStream_t s, bool pdl, const SampleParams& p, int nreq) {
   SampleParams copy = p;
   void* args[] = {&copy};
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nreq);
-  cfg.blockDim = dim3(kSampleThreads);
-  cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nreq, kPrepChunks);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.dynamicSmemBytes = ((size_t)p.vocab / kPrepChunks + 8) * sizeof(float);
+  cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (cfg.dynamicSmemBytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute((const void*)sample_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)cfg.dynamicSmemBytes);
+    if (e != cudaSuccess) return e;
+  }
+  cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)sample_prep_kernel, args);
+  if (e != cudaSuccess) return e;
+  cfg = cudaLaunchConfig_t{};
+  cfg.gridDim = dim3(nreq);
+  cfg.blockDim = dim3(kSampleThreads);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelExC(&cfg, (const void*)sample_kernel, args);
 }
 
