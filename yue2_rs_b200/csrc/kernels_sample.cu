@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(kPrepThreads) sample_prep_kernel(const SampleP
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
   __shared__ unsigned long long cand[kCand];
+  __shared__ unsigned long long cand2[kCand];  // rank-sorted copy of cand; later per-survivor scratch
   __shared__ float es[kCand];
   __shared__ uint32_t hist[256];
   __shared__ int s_count, s_nkeep;
@@ -333,6 +334,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     __syncthreads();  // every thread has read cand[jj] before it is overwritten
     auto take = [&](bool keep, float s, int i) {
       const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      if (bal == 0) return;  // warp-uniform: candidates are rare
       int base = 0;
       if (lane == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
       base = __shfl_sync(0xffffffffu, base, 0);
@@ -365,20 +367,35 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   int n = -1;
   unsigned long long* srt = nullptr;
   if (ncand > rank && ncand <= kCand) {
-    int m = 1;
-    while (m < ncand) m <<= 1;
-    for (int i = ncand + tid; i < m; i += nt) cand[i] = ~0ull;
-    __syncthreads();
-    bitonic_sort(cand, m);
-    const uint32_t thr_key = ~(uint32_t)(cand[rank] >> 32);
+    if (ncand <= kSampleThreads) {
+      // rank sort: the keys are distinct (they hold the id), so an element's position is
+      // the number of smaller keys; one pass instead of a bitonic network
+      if (tid < ncand) {
+        const unsigned long long key = cand[tid];
+        int r = 0;
+        for (int j = 0; j < ncand; ++j) r += cand[j] < key ? 1 : 0;
+        cand2[r] = key;
+      }
+      __syncthreads();
+      srt = cand2;
+    } else {
+      int m = 1;
+      while (m < ncand) m <<= 1;
+      for (int i = ncand + tid; i < m; i += nt) cand[i] = ~0ull;
+      __syncthreads();
+      bitonic_sort(cand, m);
+      srt = cand;
+    }
+    const uint32_t thr_key = ~(uint32_t)(srt[rank] >> 32);
     // a +-0 threshold: IEEE `>=` (retain, :173) and key order differ there; general path
     if (thr_key != 0x80000000u && thr_key != 0x7fffffffu) {
       int mine = 0;
-      for (int i = tid; i < ncand; i += nt) mine += (~(uint32_t)(cand[i] >> 32)) >= thr_key ? 1 : 0;
+      for (int i = tid; i < ncand; i += nt) mine += (~(uint32_t)(srt[i] >> 32)) >= thr_key ? 1 : 0;
       atomicAdd(&s_nkeep, mine);
       __syncthreads();
       n = s_nkeep;
-      srt = cand;
+    } else {
+      srt = nullptr;
     }
   }
   if (n < 0) {
@@ -468,24 +485,75 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   if (c.top_p < 1.f) {
     if (lane == 0) {
       float sum = 0.f;
-      for (int i = 0; i < n; ++i) sum += E[i];
-      float cumulative = 0.f;
-      const int protect = legacy ? 3 : 1;
-      int w = 0;
-      for (int i = 0; i < n; ++i) {
-        const float pr = cast(E[i] / sum, legacy);
-        cumulative += pr;
-        const float prior = cast(cast(cumulative, legacy) - pr, legacy);
-        if (prior <= c.top_p || i < protect) {
-          srt[w] = srt[i];
-          E[w] = E[i];
-          ++w;
-        }
-      }
-      s_nkeep = w;
+      for (int i = 0; i < n; ++i) sum += E[i];  // the reference's order
+      s_sum = sum;
     }
     __syncwarp();
-    nkeep = s_nkeep;
+    const float sum = s_sum;
+    const int protect = legacy ? 3 : 1;
+    if (n <= kCand && (srt == cand || srt == cand2)) {
+      // the probabilities in parallel; only the cumulative sum runs in order on one lane.
+      // Scratch: whichever candidate buffer does not hold the sorted survivors.
+      unsigned long long* scratch = srt == cand2 ? cand : cand2;
+      float* pr = reinterpret_cast<float*>(scratch);
+      uint32_t* keep = reinterpret_cast<uint32_t*>(scratch) + kCand;  // bit i: survivor i kept
+      for (int i = lane; i < n; i += 32) pr[i] = cast(E[i] / sum, legacy);
+      __syncwarp();
+      if (lane == 0) {
+        float cumulative = 0.f;
+        uint32_t bits = 0;
+        for (int i = 0; i < n; ++i) {
+          cumulative += pr[i];
+          const float prior = cast(cast(cumulative, legacy) - pr[i], legacy);
+          if (prior <= c.top_p || i < protect) bits |= 1u << (i & 31);
+          if ((i & 31) == 31 || i == n - 1) {
+            keep[i >> 5] = bits;
+            bits = 0;
+          }
+        }
+      }
+      __syncwarp();
+      // order-preserving compaction, 32 survivors at a time
+      int w = 0;
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const uint32_t bits = keep[i0 >> 5];
+        const int i = i0 + lane;
+        const bool k = i < n && ((bits >> lane) & 1u);
+        unsigned long long key = 0;
+        float e = 0.f;
+        if (k) {
+          key = srt[i];
+          e = E[i];
+        }
+        __syncwarp();  // every lane has read its element before any is overwritten
+        if (k) {
+          const int dst = w + __popc(bits & ((1u << lane) - 1));
+          srt[dst] = key;
+          E[dst] = e;
+        }
+        w += __popc(bits);
+        __syncwarp();
+      }
+      nkeep = w;
+    } else {
+      if (lane == 0) {
+        float cumulative = 0.f;
+        int w = 0;
+        for (int i = 0; i < n; ++i) {
+          const float pr = cast(E[i] / sum, legacy);
+          cumulative += pr;
+          const float prior = cast(cast(cumulative, legacy) - pr, legacy);
+          if (prior <= c.top_p || i < protect) {
+            srt[w] = srt[i];
+            E[w] = E[i];
+            ++w;
+          }
+        }
+        s_nkeep = w;
+      }
+      __syncwarp();
+      nkeep = s_nkeep;
+    }
   }
   if (lane == 0) {
     float sum = 0.f;
