@@ -178,27 +178,20 @@ def main():
         return run_reference(args)
 
     import torch
-    import torch.distributed as dist
     from yue2_rs_b200 import Model, Phase, Request, Session, generate_batch, synth, _lib
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+    from yue2_rs_b200.dp import DataParallel
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dp = DataParallel("nccl")
+    rank, world = dp.rank, dp.world
 
     def barrier():
-        if world > 1:
-            dist.barrier()
+        dp.barrier()
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dp.max(x)
 
     cfg = synth.config_c2()
     model = Model.synthetic(cfg, seed=1, std=0.02, device=local)
@@ -344,8 +337,7 @@ def main():
     model.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
-    if world > 1:
-        dist.destroy_process_group()
+    dp.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
