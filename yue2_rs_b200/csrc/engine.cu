@@ -115,6 +115,7 @@ Yue2Model::~Yue2Model() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  y2::free_prefill(prefill);
   for (auto& e : row_events)
     if (e) cudaEventDestroy(e);
   pool.clear();
@@ -252,6 +253,11 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   m->use_pdl = env_int("YUE2_CUDA_PDL", 1) != 0;
   m->use_graphs = env_int("YUE2_CUDA_GRAPHS", 1) != 0;
   m->use_step = env_int("YUE2_CUDA_STEP", 0) != 0;
+  {
+    const char* v = getenv("YUE2_CUDA_PREFILL");
+    m->use_prefill_gemm = !(v && std::string(v) == "gemv");
+    m->prefill_chunk = std::max(16, std::min(kPrefillRows, env_int("YUE2_CUDA_PREFILL_CHUNK", kPrefillRows)));
+  }
   *out = m;
   return 0;
 }
@@ -524,6 +530,13 @@ int check_phase_vocab(const Yue2Model& m, int phase) {
 // Final RMSNorm + LM head of `R` residual rows starting at x_row into logits rows [dst, dst+R).
 cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R, int dst_row, int phase,
                         const int32_t* skip) {
+  return encode_head_from(m, s, pdl, m.x + (size_t)x_row * m.g.hidden, R, dst_row, phase, skip);
+}
+
+// Final norm + LM head of R rows of hidden states at x (f32 [R, hidden]) into logits rows
+// [dst_row, dst_row + R).
+cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float* x, int R, int dst_row, int phase,
+                             const int32_t* skip) {
   const int V = m.g.vocab;
   if (phase != kPhaseVocab) {
     cudaError_t e = launch_fill_f32(s, m.logits + (size_t)dst_row * V, (size_t)R * V, -INFINITY);
@@ -534,7 +547,7 @@ cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R
   head_params(m, phase, p);
   p.K = m.g.hidden;
   p.R = R;
-  p.xf = m.x + (size_t)x_row * m.g.hidden;
+  p.xf = x;
   p.gamma = m.final_norm;
   p.eps = m.g.eps;
   p.of = m.logits + (size_t)dst_row * V;
@@ -836,10 +849,12 @@ int take_flags(Yue2Model& m) {
   return 0;
 }
 
-// Appends ids[0, n) to cache c in chunks of kMaxRows consecutive positions. The ids
-// must already be on the device. When logits_row >= 0, the last id's final-normed
-// hidden state goes through the LM head into logits row `logits_row`.
+// Appends ids[0, n) to cache c in chunks of kMaxRows consecutive positions (prompts of at
+// least kPrefillGemmMin ids: as GEMMs, prefill.cu). The ids must already be on the
+// device. When logits_row >= 0, the last id's final-normed hidden state goes through
+// the LM head into logits row `logits_row`.
 int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
+  if (m.use_prefill_gemm && n >= (uint64_t)kPrefillGemmMin) return prefill_gemm(m, c, d_ids, n, logits_row, phase);
   const uint64_t L0 = c.length;
   int lastR = 0;
   for (uint64_t start = 0; start < n; start += kMaxRows) {

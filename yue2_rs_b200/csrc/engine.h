@@ -32,6 +32,9 @@ struct TensorSlot {
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
+struct PrefillBufs;  // GEMM prefill workspace and cuBLASLt state (prefill.cu)
+void free_prefill(PrefillBufs* p);
+
 }  // namespace y2
 
 struct Yue2Model {
@@ -48,6 +51,9 @@ struct Yue2Model {
     unsigned* barrier = nullptr;
   };
   std::map<int, StepPlan> step_plans;  // key R * 16 + phase
+  bool use_prefill_gemm = true;  // prompts of >= kPrefillGemmMin ids as GEMMs (YUE2_CUDA_PREFILL=gemv: off)
+  int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
+  y2::PrefillBufs* prefill = nullptr;
   bool finalized = false, workspace_ready = false;
 
   char* arena = nullptr;
@@ -109,10 +115,15 @@ int check_phase_vocab(const Yue2Model& m, int phase);
 cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip);
 cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R, int dst_row, int phase,
                         const int32_t* skip);
+cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float* x, int R, int dst_row, int phase,
+                             const int32_t* skip);
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
 int prepare_step_plan(Yue2Model& m, int R, int phase);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
 int take_flags(Yue2Model& m);
 int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
+int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
+constexpr int kPrefillGemmMin = 64;  // shorter prompts go through the GEMV chain in 16-row chunks
+constexpr int kPrefillRows = 1024;   // capacity of the GEMM prefill buffers, in rows
 }  // namespace y2

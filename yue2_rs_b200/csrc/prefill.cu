@@ -1,0 +1,379 @@
+// Prompt prefill as tensor-core GEMMs (Model::prefill_phase, src/model.rs:508-522, whose
+// layer math is Model::hidden's, src/model.rs:523-591).
+//
+// A prompt of n >= kPrefillGemmMin ids is cut into equal chunks of at most
+// m.prefill_chunk (<= kPrefillRows) consecutive positions of one cache. Each chunk goes
+// through the layers with every projection as one bf16 GEMM over all of its rows
+// (cuBLASLt, f32 accumulation, bf16 output: Linear::finish's rounding,
+// src/tensor.rs:1102-1118), and small kernels for the rest:
+//   residual_norm_kernel   x = bf16(x + y) (src/tensor.rs:632-640), then Norm::apply
+//                          (src/tensor.rs:1140-1157) of the row into bf16
+//   swiglu_kernel          Mlp::apply's pointwise part (src/model.rs:206-214)
+//   rope_append_kernel     per-head QK norm + RoPE, K/V written to the cache pages
+//   attn_kernel            causal attention of every row over the paged cache
+// The last row's hidden state goes through the LM head GEMV when logits are wanted.
+#include <cublasLt.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <map>
+#include <string>
+
+#include "common.cuh"
+#include "engine.h"
+#include "kernels.h"
+
+#define CK(expr)                                          \
+  do {                                                    \
+    cudaError_t e_ = (expr);                              \
+    if (e_ != cudaSuccess) return y2::cuda_fail(e_, #expr); \
+  } while (0)
+
+namespace y2 {
+
+// ------------------------------------------------------------------ kernels
+__global__ void prefill_rows_kernel(DevRow* rows, int C, const uint64_t* pages, const int32_t* prompt,
+                                    int32_t prompt_begin, int32_t prompt_end, int32_t pos0) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= C) return;
+  DevRow r = {};
+  r.pages = pages;
+  r.prompt = prompt;
+  r.prompt_begin = prompt_begin;
+  r.prompt_end = prompt_end;
+  r.pos = pos0 + i;
+  r.active = 1;
+  r.advance = 0;
+  rows[i] = r;
+}
+
+// One row per CTA. y != nullptr: x = bf16(x + y) with y the bf16 output of the o or down
+// projection. gamma != nullptr: out = bf16(bf16(x * s) * gamma), s = bf16(1/sqrt(sum x^2
+// / H + eps)). H % 4 == 0.
+template <int NT>
+__global__ void __launch_bounds__(NT) residual_norm_kernel(float* __restrict__ x, const uint16_t* __restrict__ y,
+                                                           const float* __restrict__ gamma, int H, float eps,
+                                                           uint16_t* __restrict__ out) {
+  __shared__ float red[NT / 32];
+  const int r = blockIdx.x, tid = threadIdx.x;
+  float4* xr = reinterpret_cast<float4*>(x + (size_t)r * H);
+  const uint2* yr = y ? reinterpret_cast<const uint2*>(y + (size_t)r * H) : nullptr;
+  const int H4 = H >> 2;
+  float ss = 0.f;
+  for (int i = tid; i < H4; i += NT) {
+    float4 v = xr[i];
+    if (yr) {
+      const uint2 w = yr[i];
+      v.x = round_bf16(v.x + bf_lo(w.x));
+      v.y = round_bf16(v.y + bf_hi(w.x));
+      v.z = round_bf16(v.z + bf_lo(w.y));
+      v.w = round_bf16(v.w + bf_hi(w.y));
+      xr[i] = v;
+    }
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  if (!gamma) return;
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) t += red[w];
+  const float sc = round_bf16(1.0f / sqrtf(t / (float)H + eps));
+  const float4* gm = reinterpret_cast<const float4*>(gamma);
+  uint2* o = reinterpret_cast<uint2*>(out + (size_t)r * H);
+  for (int i = tid; i < H4; i += NT) {
+    const float4 v = xr[i], g = gm[i];
+    const uint32_t a = f2bf_exact(round_bf16(round_bf16(v.x * sc) * g.x));
+    const uint32_t b = f2bf_exact(round_bf16(round_bf16(v.y * sc) * g.y));
+    const uint32_t c = f2bf_exact(round_bf16(round_bf16(v.z * sc) * g.z));
+    const uint32_t d = f2bf_exact(round_bf16(round_bf16(v.w * sc) * g.w));
+    o[i] = make_uint2(a | (b << 16), c | (d << 16));
+  }
+}
+
+// h = bf16(bf16(silu(g)) * u) over rows of gu = [g (I columns) | u (I columns)], all bf16
+// (the GEMV's SwiGLU epilogue on GEMM outputs). I % 8 == 0.
+__global__ void swiglu_kernel(const uint16_t* __restrict__ gu, int I, int C, uint16_t* __restrict__ h) {
+  const int I8 = I >> 3;
+  const size_t total = (size_t)C * I8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / I8, c = i - r * I8;
+    const uint4 gv = ldg16(gu + r * 2 * I + c * 8);
+    const uint4 uv = ldg16(gu + r * 2 * I + I + c * 8);
+    const uint32_t* gw = &gv.x;
+    const uint32_t* uw = &uv.x;
+    uint32_t ow[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float g0 = bf_lo(gw[k]), g1 = bf_hi(gw[k]);
+      const float a0 = round_bf16(g0 / (1.0f + det_expf(-g0)));
+      const float a1 = round_bf16(g1 / (1.0f + det_expf(-g1)));
+      ow[k] = (uint32_t)f2bf_round(a0 * bf_lo(uw[k])) | ((uint32_t)f2bf_round(a1 * bf_hi(uw[k])) << 16);
+    }
+    *reinterpret_cast<uint4*>(h + r * I + c * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
+// ------------------------------------------------------------------ workspace
+struct LtGemm {
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t a = nullptr, b = nullptr, d = nullptr;
+  cublasLtMatmulAlgo_t algo{};
+};
+
+struct PrefillBufs {
+  int cap = 0;  // rows per chunk
+  float* x = nullptr;                                     // [cap, H] f32 residual stream
+  uint16_t *xb = nullptr, *qkv = nullptr, *q = nullptr;   // normed input, q|k|v, rotated q
+  uint16_t *attn = nullptr, *y = nullptr;                 // attention output, o/down output
+  uint16_t *gu = nullptr, *h = nullptr;                   // gate|up, SwiGLU output
+  DevRow* rows = nullptr;
+  float* part = nullptr;  // attention partials: cap rows x kvh x 1 split
+  int32_t* counters = nullptr;
+  cublasLtHandle_t lt = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  std::map<std::array<int, 5>, LtGemm> gemms;
+};
+
+void free_prefill(PrefillBufs* p) {
+  if (!p) return;
+  for (auto& kv : p->gemms) {
+    cublasLtMatrixLayoutDestroy(kv.second.a);
+    cublasLtMatrixLayoutDestroy(kv.second.b);
+    cublasLtMatrixLayoutDestroy(kv.second.d);
+    cublasLtMatmulDescDestroy(kv.second.op);
+  }
+  if (p->lt) cublasLtDestroy(p->lt);
+  delete p;  // device buffers are the model's allocations
+}
+
+static int lt_fail(cublasStatus_t st, const char* what) {
+  return fail(YUE2_ERR_CUDA, std::string(what) + " failed: cuBLASLt status " + std::to_string((int)st));
+}
+
+static int ensure_prefill(Yue2Model& m) {
+  if (m.prefill) return 0;
+  const Geometry& g = m.g;
+  const int C = kPrefillRows, H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
+  const int G = g.heads / g.kvh;
+  PrefillBufs* P = new PrefillBufs();
+  P->cap = C;
+  void* p = nullptr;
+  int rc;
+  auto take = [&](size_t bytes) -> void* {
+    if (rc) return nullptr;
+    rc = m.alloc(&p, bytes);
+    return rc ? nullptr : p;
+  };
+  rc = 0;
+  P->x = (float*)take((size_t)C * H * 4);
+  P->xb = (uint16_t*)take((size_t)C * H * 2);
+  P->qkv = (uint16_t*)take((size_t)C * (qd + 2 * kd) * 2);
+  P->q = (uint16_t*)take((size_t)C * qd * 2);
+  P->attn = (uint16_t*)take((size_t)C * qd * 2);
+  P->y = (uint16_t*)take((size_t)C * H * 2);
+  P->gu = (uint16_t*)take((size_t)C * 2 * I * 2);
+  P->h = (uint16_t*)take((size_t)C * I * 2);
+  P->rows = (DevRow*)take((size_t)C * sizeof(DevRow));
+  P->part = (float*)take((size_t)C * g.kvh * G * (g.dim + 2) * 4);
+  P->counters = (int32_t*)take((size_t)C * g.kvh * 4);
+  P->ws_bytes = 32u << 20;
+  P->ws = take(P->ws_bytes);
+  // buffers taken before a failure stay with the model's allocations until it closes
+  if (rc) {
+    delete P;
+    return rc;
+  }
+  cudaError_t e = cudaMemset(P->counters, 0, (size_t)C * g.kvh * 4);
+  if (e != cudaSuccess) {
+    delete P;
+    return cuda_fail(e, "prefill counters");
+  }
+  const cublasStatus_t st = cublasLtCreate(&P->lt);
+  if (st != CUBLAS_STATUS_SUCCESS) {
+    delete P;
+    return lt_fail(st, "cublasLtCreate");
+  }
+  m.prefill = P;
+  return 0;
+}
+
+// Y[C, N] (row stride ldy) = X[C, K] (row stride ldx) . W[N, K]^T, bf16 in and out, f32
+// accumulation. Algorithms that split K are excluded, so a row's result depends only on
+// the shapes (no cross-CTA reduction order).
+static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
+                     int C) {
+  PrefillBufs& P = *m.prefill;
+  const std::array<int, 5> key = {N, K, ldx, ldy, C};
+  auto it = P.gemms.find(key);
+  if (it == P.gemms.end()) {
+    LtGemm gm;
+    cublasStatus_t st;
+    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+    if ((st = cublasLtMatmulDescCreate(&gm.op, CUBLAS_COMPUTE_32F, CUDA_R_32F)) ||
+        (st = cublasLtMatmulDescSetAttribute(gm.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta))) ||
+        (st = cublasLtMatmulDescSetAttribute(gm.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb))) ||
+        (st = cublasLtMatrixLayoutCreate(&gm.a, CUDA_R_16BF, K, N, K)) ||
+        (st = cublasLtMatrixLayoutCreate(&gm.b, CUDA_R_16BF, K, C, ldx)) ||
+        (st = cublasLtMatrixLayoutCreate(&gm.d, CUDA_R_16BF, N, C, ldy)))
+      return lt_fail(st, "cuBLASLt descriptor");
+    cublasLtMatmulPreference_t pref = nullptr;
+    const uint32_t no_split = CUBLASLT_REDUCTION_SCHEME_NONE;
+    cublasLtMatmulHeuristicResult_t res{};
+    int found = 0;
+    if ((st = cublasLtMatmulPreferenceCreate(&pref)) ||
+        (st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &P.ws_bytes,
+                                                   sizeof(P.ws_bytes))) ||
+        (st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_REDUCTION_SCHEME_MASK, &no_split,
+                                                   sizeof(no_split))) ||
+        (st = cublasLtMatmulAlgoGetHeuristic(P.lt, gm.op, gm.a, gm.b, gm.d, gm.d, pref, 1, &res, &found))) {
+      if (pref) cublasLtMatmulPreferenceDestroy(pref);
+      return lt_fail(st, "cuBLASLt heuristic");
+    }
+    cublasLtMatmulPreferenceDestroy(pref);
+    if (found < 1) return fail(YUE2_ERR_CUDA, "cuBLASLt has no algorithm for a prefill GEMM");
+    gm.algo = res.algo;
+    it = P.gemms.emplace(key, gm).first;
+  }
+  const LtGemm& gm = it->second;
+  const float alpha = 1.f, beta = 0.f;
+  const cublasStatus_t st = cublasLtMatmul(P.lt, gm.op, &alpha, W, gm.a, X, gm.b, &beta, Y, gm.d, Y, gm.d, &gm.algo,
+                                           P.ws, P.ws_bytes, m.stream);
+  if (st != CUBLAS_STATUS_SUCCESS) return lt_fail(st, "cublasLtMatmul");
+  return 0;
+}
+
+// Several weight matrices [N_i, K] side by side in one output of row stride ldy: one GEMM
+// when they are adjacent in memory (the model's arena places them so), else one each.
+static int gemm_concat(Yue2Model& m, const uint16_t* const* W, const int* N, int parts, int K, const uint16_t* X,
+                       int ldx, uint16_t* Y, int ldy, int C) {
+  bool adjacent = true;
+  int total = N[0];
+  for (int i = 1; i < parts; ++i) {
+    adjacent = adjacent && W[i] == W[i - 1] + (size_t)N[i - 1] * K;
+    total += N[i];
+  }
+  if (adjacent) return gemm_bf16(m, W[0], total, K, X, ldx, Y, ldy, C);
+  int col = 0;
+  for (int i = 0; i < parts; ++i) {
+    const int rc = gemm_bf16(m, W[i], N[i], K, X, ldx, Y + col, ldy, C);
+    if (rc) return rc;
+    col += N[i];
+  }
+  return 0;
+}
+
+static cudaError_t launch_residual_norm(cudaStream_t s, float* x, const uint16_t* y, const float* gamma, int H,
+                                        float eps, uint16_t* out, int C) {
+  void* args[] = {&x, &y, &gamma, &H, &eps, &out};
+  return launch_with(s, false, dim3(C), dim3(256), 0, (const void*)residual_norm_kernel<256>, args);
+}
+
+// ------------------------------------------------------------------ one chunk, all layers
+static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t L0, uint64_t n, uint64_t start,
+                         int C) {
+  PrefillBufs& P = *m.prefill;
+  const Geometry& g = m.g;
+  const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
+  cudaStream_t s = m.stream;
+  int rc;
+  {
+    DevRow* rows = P.rows;
+    const uint64_t* pages = c.d_pages;
+    int32_t pb = (int32_t)L0, pe = (int32_t)(L0 + n), p0 = (int32_t)(L0 + start);
+    void* args[] = {&rows, &C, &pages, &d_ids, &pb, &pe, &p0};
+    CK(launch_with(s, false, dim3((C + 127) / 128), dim3(128), 0, (const void*)prefill_rows_kernel, args));
+  }
+  CK(launch_embed(s, false, P.rows, C, m.embed, H, g.vocab, P.x, m.flags + 0));
+  // one wave of attention CTAs where the chunk is short; the partials hold cap rows x kvh
+  const int splits = std::max(1, std::min(std::min(m.max_splits, P.cap / C), 2 * m.sms / (g.kvh * C)));
+  for (int l = 0; l < g.layers; ++l) {
+    const LayerW& w = m.layers[l];
+    CK(launch_residual_norm(s, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, C));
+    {
+      const uint16_t* W[3] = {w.q, w.k, w.v};
+      const int N[3] = {qd, kd, kd};
+      if ((rc = gemm_concat(m, W, N, 3, H, P.xb, H, P.qkv, qd + 2 * kd, C))) return rc;
+    }
+    RopeParams rp = {};
+    rp.rows = P.rows;
+    rp.qkv = P.qkv;
+    rp.q_out = P.q;
+    rp.cos_tab = m.cos_tab;
+    rp.sin_tab = m.sin_tab;
+    rp.q_norm = w.q_norm;
+    rp.k_norm = w.k_norm;
+    rp.g = g;
+    rp.layer = l;
+    rp.max_pos = m.max_pos;
+    rp.error = m.flags + 1;
+    CK(launch_rope_append(s, false, rp, C));
+    AttnParams ap = {};
+    ap.rows = P.rows;
+    ap.q = P.q;
+    ap.out = P.attn;
+    ap.part = P.part;
+    ap.counters = P.counters;
+    ap.g = g;
+    ap.layer = l;
+    ap.splits = splits;
+    ap.scale = 1.0f / sqrtf((float)g.dim);
+    ap.fused = 0;
+    ap.qkv = P.qkv;
+    ap.q_norm = w.q_norm;
+    ap.k_norm = w.k_norm;
+    ap.cos_tab = m.cos_tab;
+    ap.sin_tab = m.sin_tab;
+    ap.max_pos = m.max_pos;
+    ap.error = m.flags + 1;
+    CK(launch_attention(s, false, ap, C));
+    if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, C))) return rc;
+    CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, C));
+    {
+      const uint16_t* W[2] = {w.gate, w.up};
+      const int N[2] = {I, I};
+      if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, C))) return rc;
+    }
+    {
+      const uint16_t* gu = P.gu;
+      uint16_t* h = P.h;
+      int inter = I, rows = C;
+      void* args[] = {&gu, &inter, &rows, &h};
+      const int blocks = std::min(4 * m.sms, (int)(((size_t)C * (I / 8) + 255) / 256));
+      CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)swiglu_kernel, args));
+    }
+    if ((rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, C))) return rc;
+  }
+  // the last layer's residual (the LM head applies the final norm itself)
+  CK(launch_residual_norm(s, P.x, P.y, nullptr, H, g.eps, nullptr, C));
+  return 0;
+}
+
+int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
+  const Geometry& g = m.g;
+  if (g.hidden % 8 || g.inter % 8 || (g.heads * g.dim) % 8 || g.dim % 8)
+    return fail(YUE2_ERR_INVALID, "GEMM prefill needs hidden, intermediate and head sizes divisible by 8");
+  int rc = ensure_prefill(m);
+  if (rc) return rc;
+  const uint64_t L0 = c.length;
+  const uint64_t chunks = (n + m.prefill_chunk - 1) / m.prefill_chunk;
+  const uint64_t per = (n + chunks - 1) / chunks;
+  int lastC = 0;
+  for (uint64_t start = 0; start < n; start += per) {
+    const int C = (int)std::min<uint64_t>(per, n - start);
+    if ((rc = prefill_chunk(m, c, d_ids, L0, n, start, C))) return rc;
+    lastC = C;
+  }
+  if (logits_row >= 0)
+    CK(encode_head_from(m, m.stream, false, m.prefill->x + (size_t)(lastC - 1) * g.hidden, 1, logits_row, phase,
+                        nullptr));
+  c.length = L0 + n;
+  return 0;
+}
+
+}  // namespace y2
