@@ -332,7 +332,8 @@ def main():
         "ctx_sweep": sweep,
         "batched": batched,
         "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "prefill_seconds": outs[0].prefill_seconds,
+                "prefill_seconds": outs[0].prefill_seconds, "library_seconds": outs[0].seconds,
+                "decode_ms": outs[0].decode_ms,
                 "what": "yue2_generate: 512 tokens per song incl. both 1,024-id prefills, host buffers in/out"},
     }
     model.close()

@@ -5,6 +5,8 @@ positions, Model::prefill_phase, src/model.rs:508-522).
     later chunks attend to K/V written by earlier ones;
   * against the GEMV prefill (YUE2_CUDA_PREFILL=gemv) on the unit-gain model: same math,
     other f32 summation order;
+  * the tensor-core causal attention against the per-row decode attention kernel
+    (YUE2_CUDA_PREFILL_ATTN=rows) over a 1,000-id prompt in chunks of 250 positions;
   * appending to a non-empty cache, and run-to-run determinism (bit-exact logits and K/V).
 """
 import os
@@ -36,6 +38,20 @@ def _open(path, **env):
 @pytest.fixture(scope="module")
 def chunked(c1_dir):
     m = _open(c1_dir, YUE2_CUDA_PREFILL_CHUNK=96)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def rows_u(c1u_dir):
+    m = _open(c1u_dir, YUE2_CUDA_PREFILL_ATTN="rows", YUE2_CUDA_PREFILL_CHUNK=300)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def chunk300_u(c1u_dir):
+    m = _open(c1u_dir, YUE2_CUDA_PREFILL_CHUNK=300)
     yield m
     m.close()
 
@@ -113,3 +129,23 @@ def test_gemm_prefill_is_deterministic(c1u_device, c1_prompt):
         ka, va = ca.read(layer, 0, len(prompt))
         kb, vb = cb.read(layer, 0, len(prompt))
         assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+
+
+def test_tensor_core_attention_matches_row_attention(chunk300_u, rows_u, c1_config):
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, c1_config.vocab_size, 1000).tolist()
+    teacher = rng.integers(0, c1_config.vocab_size, 4).tolist()
+    a, ca = _decode(chunk300_u, prompt, teacher)
+    b, cb = _decode(rows_u, prompt, teacher)
+    assert np.isfinite(a).all()
+    assert np.abs(a - b).max() <= 0.08 and np.abs(a - b).mean() <= 1e-2
+    assert (a.argmax(-1) == b.argmax(-1)).mean() >= 0.9
+    # layer 0's K/V do not depend on attention; layer 1's inherit its summation order
+    ka, va = ca.read(0, 0, len(prompt))
+    kb, vb = cb.read(0, 0, len(prompt))
+    assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    to_f = lambda x: (x.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    ka, va = ca.read(1, 0, len(prompt))
+    kb, vb = cb.read(1, 0, len(prompt))
+    for x, y in ((ka, kb), (va, vb)):
+        assert np.linalg.norm(to_f(x) - to_f(y)) <= 2e-2 * np.linalg.norm(to_f(y))

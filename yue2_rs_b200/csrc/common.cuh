@@ -51,6 +51,35 @@ Y2_DEV void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// 16-byte async copy that writes zeros instead when !valid (no global read then).
+Y2_DEV void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(valid ? 16 : 0) : "memory");
+}
+
+// Four 8x8 b16 matrices from shared memory; lane i gives the address of row i % 8 of
+// matrix i / 8, and register j receives this lane's fragment of matrix j.
+Y2_DEV void ldsm_x4(uint32_t (&r)[4], const void* smem) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+// The same with each matrix transposed.
+Y2_DEV void ldsm_x4_trans(uint32_t (&r)[4], const void* smem) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+// Two f32 to a bf16x2 word (round to nearest even; lo in the low half).
+Y2_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // D += A(16x16, row) * B(16x8, col), bf16 in, f32 accumulate
 Y2_DEV void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                            uint32_t b1) {

@@ -257,6 +257,8 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     const char* v = getenv("YUE2_CUDA_PREFILL");
     m->use_prefill_gemm = !(v && std::string(v) == "gemv");
     m->prefill_chunk = std::max(16, std::min(kPrefillRows, env_int("YUE2_CUDA_PREFILL_CHUNK", kPrefillRows)));
+    const char* a = getenv("YUE2_CUDA_PREFILL_ATTN");
+    m->prefill_tc_attn = !(a && std::string(a) == "rows");
   }
   *out = m;
   return 0;

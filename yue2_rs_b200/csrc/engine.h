@@ -53,6 +53,7 @@ struct Yue2Model {
   std::map<int, StepPlan> step_plans;  // key R * 16 + phase
   bool use_prefill_gemm = true;  // prompts of >= kPrefillGemmMin ids as GEMMs (YUE2_CUDA_PREFILL=gemv: off)
   int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
+  bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
   y2::PrefillBufs* prefill = nullptr;
   bool finalized = false, workspace_ready = false;
 

@@ -90,6 +90,17 @@ struct AttnParams {
   int32_t* error;
 };
 
+// Causal attention of a prefill chunk: rows [0, C) at positions pos0 + row of one cache,
+// whose K/V (those rows' included) are already in the pages.
+struct PrefillAttnParams {
+  const uint64_t* pages;  // the cache's page table
+  const uint16_t* q;      // rotated queries [C, heads*dim] bf16
+  uint16_t* out;          // [C, heads*dim] bf16
+  Geometry g;
+  int layer, C, pos0;
+  float scale;
+};
+
 struct RopeParams {
   const DevRow* rows;
   const uint16_t* qkv;   // [R, (heads + 2 kvh) * dim] bf16
@@ -185,6 +196,8 @@ cudaError_t launch_gemv_tc(cudaStream_t s, bool pdl, int xmode, int epi, const G
 cudaError_t launch_with(cudaStream_t s, bool pdl, dim3 grid, dim3 block, size_t smem, const void* fn, void** args);
 cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R);
 cudaError_t launch_attention(cudaStream_t s, bool pdl, const AttnParams& p, int R);
+bool prefill_attention_supported(const Geometry& g);
+cudaError_t launch_prefill_attention(cudaStream_t s, const PrefillAttnParams& p);
 cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R);
 cudaError_t launch_mt_words(cudaStream_t s, MtState* st, uint32_t* words, int nwords, const SampleReq* reqs,
                             int nreq);

@@ -10,7 +10,9 @@
 //                          (src/tensor.rs:1140-1157) of the row into bf16
 //   swiglu_kernel          Mlp::apply's pointwise part (src/model.rs:206-214)
 //   rope_append_kernel     per-head QK norm + RoPE, K/V written to the cache pages
-//   attn_kernel            causal attention of every row over the paged cache
+//   prefill_attn_kernel    causal attention of the chunk's rows over the paged cache on
+//                          the tensor cores (kernels_prefill_attn.cu); head sizes it does
+//                          not take (and YUE2_CUDA_PREFILL_ATTN=rows) use attn_kernel per row
 // The last row's hidden state goes through the LM head GEMV when logits are wanted.
 #include <cublasLt.h>
 #include <cuda_runtime.h>
@@ -274,6 +276,33 @@ static cudaError_t launch_residual_norm(cudaStream_t s, float* x, const uint16_t
   return launch_with(s, false, dim3(C), dim3(256), 0, (const void*)residual_norm_kernel<256>, args);
 }
 
+// Per-row split-K decode attention over the chunk's rows (head sizes the tensor-core
+// kernel does not take).
+static int row_attention(Yue2Model& m, PrefillBufs& P, int l, int C, int splits) {
+  const LayerW& w = m.layers[l];
+  const Geometry& g = m.g;
+  AttnParams ap = {};
+  ap.rows = P.rows;
+  ap.q = P.q;
+  ap.out = P.attn;
+  ap.part = P.part;
+  ap.counters = P.counters;
+  ap.g = g;
+  ap.layer = l;
+  ap.splits = splits;
+  ap.scale = 1.0f / sqrtf((float)g.dim);
+  ap.fused = 0;
+  ap.qkv = P.qkv;
+  ap.q_norm = w.q_norm;
+  ap.k_norm = w.k_norm;
+  ap.cos_tab = m.cos_tab;
+  ap.sin_tab = m.sin_tab;
+  ap.max_pos = m.max_pos;
+  ap.error = m.flags + 1;
+  CK(launch_attention(m.stream, false, ap, C));
+  return 0;
+}
+
 // ------------------------------------------------------------------ one chunk, all layers
 static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t L0, uint64_t n, uint64_t start,
                          int C) {
@@ -313,25 +342,20 @@ static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint6
     rp.max_pos = m.max_pos;
     rp.error = m.flags + 1;
     CK(launch_rope_append(s, false, rp, C));
-    AttnParams ap = {};
-    ap.rows = P.rows;
-    ap.q = P.q;
-    ap.out = P.attn;
-    ap.part = P.part;
-    ap.counters = P.counters;
-    ap.g = g;
-    ap.layer = l;
-    ap.splits = splits;
-    ap.scale = 1.0f / sqrtf((float)g.dim);
-    ap.fused = 0;
-    ap.qkv = P.qkv;
-    ap.q_norm = w.q_norm;
-    ap.k_norm = w.k_norm;
-    ap.cos_tab = m.cos_tab;
-    ap.sin_tab = m.sin_tab;
-    ap.max_pos = m.max_pos;
-    ap.error = m.flags + 1;
-    CK(launch_attention(s, false, ap, C));
+    if (m.prefill_tc_attn && prefill_attention_supported(g)) {
+      PrefillAttnParams fp = {};
+      fp.pages = c.d_pages;
+      fp.q = P.q;
+      fp.out = P.attn;
+      fp.g = g;
+      fp.layer = l;
+      fp.C = C;
+      fp.pos0 = (int)(L0 + start);
+      fp.scale = 1.0f / sqrtf((float)g.dim);
+      CK(launch_prefill_attention(s, fp));
+    } else if ((rc = row_attention(m, P, l, C, splits))) {
+      return rc;
+    }
     if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, C))) return rc;
     CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, C));
     {
