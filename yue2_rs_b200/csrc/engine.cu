@@ -128,6 +128,26 @@ Yue2Model::~Yue2Model() {
   if (ev_join) cudaEventDestroy(ev_join);
 }
 
+// The smallest cached buffer of at least `bytes` (and at most twice that), else a new one.
+int Yue2Model::scratch_take(void** p, size_t bytes) {
+  bytes = (bytes + 255) & ~(size_t)255;
+  auto it = scratch_free.lower_bound(bytes);
+  if (it != scratch_free.end() && it->first <= 2 * bytes) {
+    *p = it->second;
+    scratch_free.erase(it);
+    return 0;
+  }
+  const int rc = alloc(p, bytes);
+  if (!rc) scratch_cap[*p] = bytes;
+  return rc;
+}
+
+void Yue2Model::scratch_give(void* p) {
+  if (!p) return;
+  auto it = scratch_cap.find(p);
+  if (it != scratch_cap.end()) scratch_free.emplace(it->second, p);
+}
+
 int Yue2Model::alloc(void** p, size_t bytes) {
   cudaError_t e = cudaMalloc(p, bytes);
   if (e != cudaSuccess) {
@@ -423,13 +443,14 @@ int yue2_cache_create(Yue2Model* m, uint64_t capacity, Yue2Cache** out) {
     delete c;
     return rc;
   }
-  cudaError_t e = cudaMalloc(&c->d_pages, npages * 8);
-  if (e != cudaSuccess) {
+  void* pt = nullptr;
+  if ((rc = m->scratch_take(&pt, npages * 8))) {
     m->pool.give(c->pages);
     delete c;
-    return cuda_fail(e, "page table");
+    return rc;
   }
-  e = cudaMemcpy(c->d_pages, c->pages.data(), npages * 8, cudaMemcpyHostToDevice);
+  c->d_pages = (uint64_t*)pt;
+  cudaError_t e = cudaMemcpy(c->d_pages, c->pages.data(), npages * 8, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     yue2_cache_free(c);
     return cuda_fail(e, "page table upload");
@@ -441,8 +462,10 @@ int yue2_cache_create(Yue2Model* m, uint64_t capacity, Yue2Cache** out) {
 void yue2_cache_free(Yue2Cache* c) {
   if (!c) return;
   cudaSetDevice(c->m->device);
+  // work queued on the model's stream may still use the pages and the page table
+  if (c->m->stream) cudaStreamSynchronize(c->m->stream);
   c->m->pool.give(c->pages);
-  if (c->d_pages) cudaFree(c->d_pages);
+  c->m->scratch_give(c->d_pages);
   delete c;
 }
 
@@ -936,11 +959,12 @@ int yue2_prefill(Yue2Model* m, Yue2Cache* c, const int64_t* ids, uint64_t n, int
     h[i] = (int32_t)ids[i];
   }
   if ((rc = y2_set_device(m))) return rc;
-  int32_t* d_ids = nullptr;
-  CK(cudaMalloc(&d_ids, n * 4));
+  void* ids_mem = nullptr;
+  if ((rc = m->scratch_take(&ids_mem, n * 4))) return rc;
+  int32_t* d_ids = (int32_t*)ids_mem;
   cudaError_t e = cudaMemcpy(d_ids, h.data(), n * 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
-    cudaFree(d_ids);
+    m->scratch_give(d_ids);
     return cuda_fail(e, "prefill ids");
   }
   const uint64_t before = c->length;
@@ -951,7 +975,7 @@ int yue2_prefill(Yue2Model* m, Yue2Cache* c, const int64_t* ids, uint64_t n, int
   }
   if (!rc) rc = take_flags(*m);
   cudaStreamSynchronize(m->stream);
-  cudaFree(d_ids);
+  m->scratch_give(d_ids);
   if (rc) c->length = before;
   return rc;
 }

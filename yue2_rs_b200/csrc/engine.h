@@ -88,8 +88,15 @@ struct Yue2Model {
 
   std::map<int, cudaGraphExec_t> graphs;
   std::vector<void*> allocations;
+  // Device scratch reused across calls (sampler buffers, prompt uploads, page tables):
+  // cudaFree can stall the host for hundreds of milliseconds, so finished calls return
+  // their buffers here; they are freed with the model.
+  std::multimap<size_t, void*> scratch_free;
+  std::map<void*, size_t> scratch_cap;
 
   int alloc(void** p, size_t bytes);
+  int scratch_take(void** p, size_t bytes);
+  void scratch_give(void* p);
   int max_pos_limit() const {
     return (int)(cfg.max_position_embeddings < (1u << 20) ? cfg.max_position_embeddings : (1u << 20));
   }

@@ -87,20 +87,19 @@ struct SamplerBufs {
   int32_t* flags = nullptr;  // [0] live requests, [1] all done
   SampleAcc* acc = nullptr;
   int sort_cap = 0;
-  std::vector<void*> owned;
+  Yue2Model* m = nullptr;
+  std::vector<void*> owned;  // the model's scratch buffers, returned on destruction
 
-  int alloc(size_t n, size_t V, size_t max_tokens, bool need_words) {
+  int get(void** p, size_t bytes) {
+    const int rc = m->scratch_take(p, bytes);
+    if (!rc) owned.push_back(*p);
+    return rc;
+  }
+
+  int alloc(Yue2Model* model, size_t n, size_t V, size_t max_tokens, bool need_words) {
+    m = model;
     sort_cap = 1;
     while ((size_t)sort_cap < V) sort_cap <<= 1;
-    auto get = [&](void** p, size_t bytes) -> int {
-      cudaError_t e = cudaMalloc(p, bytes);
-      if (e != cudaSuccess) {
-        cudaGetLastError();
-        return fail(YUE2_ERR_OOM, "sampler scratch allocation failed");
-      }
-      owned.push_back(*p);
-      return 0;
-    };
     int rc;
     if ((rc = get((void**)&reqs, n * sizeof(SampleReq))) || (rc = get((void**)&tokens, n * max_tokens * 4 + 4)) ||
         (rc = get((void**)&mt, n * sizeof(MtState))) || (rc = get((void**)&scores, n * V * 4)) ||
@@ -117,7 +116,7 @@ struct SamplerBufs {
     return 0;
   }
   ~SamplerBufs() {
-    for (void* p : owned) cudaFree(p);
+    for (void* p : owned) m->scratch_give(p);
   }
 };
 
@@ -232,10 +231,9 @@ int yue2_choose(Yue2Model* m, const float* logits, uint64_t vocab, const Yue2Sam
   if ((rc = y2_set_device(m))) return rc;
   SamplerBufs b;
   const bool draw = s->temperature != 0.f;
-  if ((rc = b.alloc(1, vocab, hlen + 1, draw))) return rc;
+  if ((rc = b.alloc(m, 1, vocab, hlen + 1, draw))) return rc;
   float* d_logits = nullptr;
-  CK(cudaMalloc(&d_logits, vocab * 4));
-  b.owned.push_back(d_logits);
+  if ((rc = b.get((void**)&d_logits, vocab * 4))) return rc;
   CK(cudaMemcpy(d_logits, logits, vocab * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(b.tokens, hist.data(), hist.size() * 4, cudaMemcpyHostToDevice));
   SampleReq q = {};
@@ -305,7 +303,8 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
   int row = 0;
   std::vector<int32_t*> d_prompts;
   auto free_prompts = [&]() {
-    for (int32_t* p : d_prompts) cudaFree(p);
+    cudaStreamSynchronize(m->stream);  // queued prefills may still read them
+    for (int32_t* p : d_prompts) m->scratch_give(p);
   };
   for (uint64_t i = 0; i < n; ++i) {
     const Yue2Request& q = reqs[i];
@@ -332,12 +331,12 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
         h[j] = (int32_t)ids[j];
       }
       int32_t* d = nullptr;
-      cudaError_t e = cudaMalloc(&d, len * 4);
-      if (e != cudaSuccess) {
+      if ((rc = m->scratch_take((void**)&d, len * 4))) {
         free_prompts();
-        return bail(cuda_fail(e, "prompt upload"));
+        return bail(rc);
       }
       d_prompts.push_back(d);
+      cudaError_t e;
       if ((e = cudaMemcpy(d, h.data(), len * 4, cudaMemcpyHostToDevice)) != cudaSuccess) {
         free_prompts();
         return bail(cuda_fail(e, "prompt upload"));
@@ -360,7 +359,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
   // ---- sampler state
   const int V = m->g.vocab;
   const bool draw = s->temperature != 0.f;
-  if ((rc = ss->bufs.alloc(n, V, s->max_tokens, draw))) return bail(rc);
+  if ((rc = ss->bufs.alloc(m, n, V, s->max_tokens, draw))) return bail(rc);
   std::vector<SampleReq> hq(n);
   std::vector<MtState> hm(n);
   for (uint64_t i = 0; i < n; ++i) {
