@@ -173,6 +173,12 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="decode steps only (16-id prompts; no sweep, e2e, kernel hook or CPU baseline): "
                          "the command line for ncu launch lists")
+    ap.add_argument("--profile-songs", type=int, default=1, metavar="B",
+                    help="with --profile: B songs (2B CFG rows) of 16-id prompts after a synthetic "
+                         "1,008-position context")
+    ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
+                    help="one N-id prefill of the config-1 model and exit: the command line for the "
+                         "prefill's ncu launch list")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -195,16 +201,31 @@ def main():
 
     cfg = synth.config_c2()
     model = Model.synthetic(cfg, seed=1, std=0.02, device=local)
+    if args.prefill_profile:
+        ids = np.random.default_rng(5).integers(0, cfg.vocab_size, args.prefill_profile).tolist()
+        c = model.new_cache(args.prefill_profile + 8)
+        model.forward(ids, c)
+        torch.cuda.synchronize()
+        c.close()
+        model.close()
+        dp.close()
+        return 0
     W, K = max(args.warmup, 3), args.steps
     max_tokens = max(512, W + K + 1)
     cond, uncond = prompts(1000 + rank, cfg.vocab_size)
+    reqs = [Request(cond, seed=rank, negative=uncond, scale=SCALE)]
     if args.profile:
-        cond, uncond = cond[:16], uncond[:16]
+        B = max(1, args.profile_songs)
+        if B == 1:
+            reqs = [Request(cond[:16], seed=rank, negative=uncond[:16], scale=SCALE)]
+        else:
+            reqs = [Request(cond[16 * i: 16 * i + 16], seed=rank + i, negative=uncond[16 * i: 16 * i + 16], scale=SCALE,
+                            context_fill=PROMPT - 16) for i in range(B)]
         args.no_sweep = args.no_cpu_baseline = True
     s = c2_sampling(max_tokens)
 
     # ---- device-resident timed region: K decode steps of one song per rank
-    sess = Session(model, [Request(cond, seed=rank, negative=uncond, scale=SCALE)], s, Phase.VOCAB)
+    sess = Session(model, reqs, s, Phase.VOCAB)
     stream = torch.cuda.ExternalStream(sess.cuda_stream)
     sess.step(W)
     sess.sync()
@@ -273,11 +294,12 @@ def main():
                              "hbm_frac_of_measured": sb / (sms / ks * 1e-3) / 1e9 / peak,
                              "hbm_frac_of_8TBs": sb / (sms / ks * 1e-3) / 8e12}
 
-    # ---- config 3 (batched songs): 8 songs of one rank in every weight pass (16 CFG rows) at
-    # a ~1,024-position context (synthetic KV fill ahead of 8-id prompts)
+    # ---- config 3 (batched songs): B songs of one rank in every pass (2B CFG rows; GEMV up to
+    # 16 rows, tensor-core GEMMs beyond) at a ~1,024-position context (synthetic KV fill
+    # ahead of 8-id prompts)
     batched = {}
-    if not args.no_sweep:
-        B, ks = 8, 24
+    for B in ((8, 32, 64) if not args.no_sweep else ()):
+        ks = 24
         mt = 4 + ks + 1
         reqs = [Request(cond[8 * i: 8 * i + 8], seed=100 * rank + i, negative=uncond[8 * i: 8 * i + 8], scale=SCALE,
                         context_fill=PROMPT - 8) for i in range(B)]
@@ -296,9 +318,10 @@ def main():
         ss.close()
         ctx = PROMPT + 5 + ks / 2.0
         sb = weight_bytes(cfg) + 2 * B * kv_bytes_per_token(cfg) * ctx
-        batched = {"songs_per_gpu": B, "rows": 2 * B, "tokens_per_s": world * B * ks / (bms / 1000.0),
-                   "ms_per_step": bms / ks, "context_mid": ctx, "step_bytes": sb,
-                   "hbm_frac_of_measured": sb / (bms / ks * 1e-3) / 1e9 / peak}
+        batched[str(B)] = {"songs_per_gpu": B, "rows": 2 * B, "tokens_per_s": world * B * ks / (bms / 1000.0),
+                           "ms_per_step": bms / ks, "context_mid": ctx, "step_bytes": sb,
+                           "hbm_frac_of_measured": sb / (bms / ks * 1e-3) / 1e9 / peak,
+                           "forward": "gemv" if 2 * B <= 16 else "gemm"}
 
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()

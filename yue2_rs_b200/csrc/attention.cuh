@@ -51,14 +51,17 @@ Y2_DEV void attn_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // CTA. STANDALONE: the attn_kernel launch (programmatic dependent launch, first tile
 // requested before the wait, splits merged by the last CTA through an atomic ticket).
 // Otherwise the caller runs after a grid-wide barrier and merges the partials itself
-// after another one (attn_merge_slice).
-template <int D, int G, bool STANDALONE>
+// after another one (attn_merge_slice). PIPE (passes of many rows, each CTA streaming
+// many tiles per warp): two K buffers per warp; the next tile's K is requested before the
+// current tile's scores and its V right after the current P.V, so loads overlap compute.
+template <int D, int G, bool STANDALONE, bool PIPE = false>
 Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned char* smem_raw) {
   constexpr int CPR = D / 8;  // 16-byte chunks per key row
   constexpr int DL = D / 32;  // dims per lane
   constexpr int NW = 4;
-  uint16_t* ktile = reinterpret_cast<uint16_t*>(smem_raw);           // [NW][32][D]
-  uint16_t* vtile = ktile + NW * 32 * D;                               // [NW][32][D]
+  constexpr int KB = PIPE ? 2 : 1;  // K tile buffers per warp
+  uint16_t* ktile = reinterpret_cast<uint16_t*>(smem_raw);           // [NW][KB][32][D]
+  uint16_t* vtile = ktile + NW * KB * 32 * D;                          // [NW][32][D]
   float* qs = reinterpret_cast<float*>(vtile + NW * 32 * D);           // [G][D]
   float* ps = qs + G * D;                                              // [NW][G][32]
   float* wm = ps + NW * G * 32;                                        // [NW][G]
@@ -80,7 +83,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   const int nsplit = (ntiles + tps - 1) / tps;
   if (split >= nsplit) return;
   const int t0 = split * tps, t1 = min(ntiles, t0 + tps);
-  uint16_t* kt = ktile + warp * 32 * D;
+  uint16_t* kt = ktile + warp * KB * 32 * D;
   uint16_t* vt = vtile + warp * 32 * D;
   const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
   auto stage = [&](int t) {  // cp.async one 32-key tile of K (swizzled) and V
@@ -101,7 +104,31 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   // the tile holding the new position is written in this launch (fused) or by the
   // preceding kernel (prefill rows): it is never fetched before the wait
   const int first_tile = t0 + warp;
-  const bool early = STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  const bool early = !PIPE && STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  // PIPE: K (swizzled) of tile t into buffer buf, V of tile t; one commit group each
+  auto stage_k = [&](int t, int buf) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
+    const uint16_t* kb = page + koff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    uint16_t* dst = kt + (size_t)buf * 32 * D;
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int j = i / CPR, c = i % CPR;
+      if (j < nk) cp_async16(dst + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
+    }
+    cp_async_commit();
+  };
+  auto stage_v = [&](int t) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
+    const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int j = i / CPR, c = i % CPR;
+      if (j < nk) cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+    }
+    cp_async_commit();
+  };
   if (early) stage(first_tile);
 
   if (STANDALONE) {
@@ -156,11 +183,22 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   }
   float* pw = ps + warp * G * 32;
 
-  for (int t = t0 + warp; t < t1; t += NW) {
+  if (PIPE && first_tile < t1) {
+    stage_k(first_tile, 0);
+    stage_v(first_tile);
+  }
+  for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
     const int key0 = t << 5;
     const int nk = min(32, keys - key0);
-    if (!(early && t == first_tile)) stage(t);
-    cp_async_wait<0>();
+    const uint16_t* kcur = kt + (PIPE ? (size_t)(it & 1) * 32 * D : 0);
+    if constexpr (PIPE) {
+      if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
+      else cp_async_commit();  // keeps the group count: K(t) is third from the end
+      cp_async_wait<2>();
+    } else {
+      if (!(early && t == first_tile)) stage(t);
+      cp_async_wait<0>();
+    }
     __syncwarp();
 
     float sc[G];
@@ -169,7 +207,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     if (lane < nk) {
 #pragma unroll 4
       for (int c = 0; c < CPR; ++c) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(kt + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
+        const uint4 kv = *reinterpret_cast<const uint4*>(kcur + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
         const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
         const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
 #pragma unroll
@@ -201,6 +239,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
 #pragma unroll
       for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
     }
+    if constexpr (PIPE) cp_async_wait<1>();  // V(t); K of the next tile may stay in flight
     __syncwarp();
     for (int j = 0; j < nk; ++j) {
       const uint16_t* vr = vt + (size_t)j * D + lane * DL;
@@ -234,7 +273,12 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
       }
     }
     __syncwarp();
+    if constexpr (PIPE) {
+      if (t + NW < t1) stage_v(t + NW);
+      else cp_async_commit();
+    }
   }
+  if constexpr (PIPE) cp_async_wait<0>();
 
   // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
   attn_sync();

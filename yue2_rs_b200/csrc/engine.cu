@@ -279,6 +279,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     m->prefill_chunk = std::max(16, std::min(kPrefillRows, env_int("YUE2_CUDA_PREFILL_CHUNK", kPrefillRows)));
     const char* a = getenv("YUE2_CUDA_PREFILL_ATTN");
     m->prefill_tc_attn = !(a && std::string(a) == "rows");
+    m->gemm_split_k = env_int("YUE2_CUDA_GEMM_SPLITK", 0) != 0;
   }
   *out = m;
   return 0;
@@ -875,7 +876,7 @@ int take_flags(Yue2Model& m) {
 }
 
 // Appends ids[0, n) to cache c in chunks of kMaxRows consecutive positions (prompts of at
-// least kPrefillGemmMin ids: as GEMMs, prefill.cu). The ids must already be on the
+// least kPrefillGemmMin ids: as GEMMs, gemm_rows.cu). The ids must already be on the
 // device. When logits_row >= 0, the last id's final-normed hidden state goes through
 // the LM head into logits row `logits_row`.
 int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
@@ -914,7 +915,7 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
                  float* logits) {
   if (!m || !caches || !ids) return fail(YUE2_ERR_INVALID, "null argument");
   if (!m->finalized) return fail(YUE2_ERR_INVALID, "model not finalized");
-  if (rows < 1 || rows > (uint64_t)kMaxRows) return fail(YUE2_ERR_INVALID, "rows must be in [1, 16]");
+  if (rows < 1 || rows > (uint64_t)kMaxWideRows) return fail(YUE2_ERR_INVALID, "rows must be in [1, 256]");
   int rc = check_phase_vocab(*m, phase);
   if (rc) return rc;
   std::set<const Yue2Cache*> seen;
@@ -936,10 +937,17 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
     dr[r].active = 1;
     dr[r].advance = 1;
   }
-  if ((rc = upload_rows(*m, dr))) return rc;
-  if ((rc = run_forward(*m, (int)rows, true, phase))) return rc;
-  if (logits)
-    CK(cudaMemcpyAsync(logits, m->logits, rows * m->g.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+  const float* out = m->logits;
+  if (rows > (uint64_t)kMaxRows) {  // the GEMM path (gemm_rows.cu)
+    if ((rc = ensure_wide(*m))) return rc;
+    CK(cudaMemcpyAsync(m->wide_rows, dr.data(), rows * sizeof(DevRow), cudaMemcpyHostToDevice, m->stream));
+    if ((rc = encode_forward_wide(*m, m->stream, (int)rows, phase))) return rc;
+    out = m->wide_logits;
+  } else {
+    if ((rc = upload_rows(*m, dr))) return rc;
+    if ((rc = run_forward(*m, (int)rows, true, phase))) return rc;
+  }
+  if (logits) CK(cudaMemcpyAsync(logits, out, rows * m->g.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
   if ((rc = take_flags(*m))) return rc;
   for (uint64_t r = 0; r < rows; ++r) caches[r]->length += 1;
   return 0;

@@ -32,7 +32,7 @@ struct TensorSlot {
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
-struct PrefillBufs;  // GEMM prefill workspace and cuBLASLt state (prefill.cu)
+struct PrefillBufs;  // GEMM workspace and cuBLASLt state (gemm_rows.cu)
 void free_prefill(PrefillBufs* p);
 
 }  // namespace y2
@@ -54,7 +54,13 @@ struct Yue2Model {
   bool use_prefill_gemm = true;  // prompts of >= kPrefillGemmMin ids as GEMMs (YUE2_CUDA_PREFILL=gemv: off)
   int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
   bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
+  bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   y2::PrefillBufs* prefill = nullptr;
+  // decode steps of more than kMaxRows rows (the GEMM path): row descriptors, logits
+  // [kMaxWideRows, vocab] and the bf16 LM head output
+  y2::DevRow* wide_rows = nullptr;
+  float* wide_logits = nullptr;
+  uint16_t* wide_head = nullptr;
   bool finalized = false, workspace_ready = false;
 
   char* arena = nullptr;
@@ -132,6 +138,10 @@ int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
 int take_flags(Yue2Model& m);
 int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
 int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
+int ensure_wide(Yue2Model& m);
+int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase);
+int wide_kernels_per_step(const Yue2Model& m, int phase);
+constexpr int kMaxWideRows = 256;    // rows of a wide decode step (128 songs with CFG)
 constexpr int kPrefillGemmMin = 64;  // shorter prompts go through the GEMV chain in 16-row chunks
 constexpr int kPrefillRows = 1024;   // capacity of the GEMM prefill buffers, in rows
 }  // namespace y2

@@ -148,6 +148,7 @@ struct Yue2Session {
   int phase = 0;
   size_t n = 0;
   int R = 0;
+  bool wide = false;  // more than kMaxRows rows: the GEMM forward
   std::vector<Yue2Cache*> caches;
   std::vector<int> cond_row, uncond_row;
   SamplerBufs bufs;
@@ -285,9 +286,11 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
       return fail(YUE2_ERR_INVALID, "Empty prefill");
     R += q.scale != 1.f ? 2 : 1;
   }
-  if (R > kMaxRows)
-    return fail(YUE2_ERR_INVALID, "at most 16 decode rows (CFG rows count twice) per session");
+  if (R > kMaxWideRows)
+    return fail(YUE2_ERR_INVALID, "at most 256 decode rows (CFG rows count twice) per session");
   if ((rc = y2_set_device(m))) return rc;
+  const bool wide = R > kMaxRows;  // the GEMM path (gemm_rows.cu) past 16 rows
+  if (wide && (rc = ensure_wide(*m))) return rc;
   Yue2Session* ss = new Yue2Session();
   ss->m = m;
   ss->s = *s;
@@ -295,6 +298,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
   ss->phase = phase;
   ss->n = n;
   ss->R = R;
+  ss->wide = wide;
   auto bail = [&](int code) {
     delete ss;
     return code;
@@ -341,9 +345,19 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
         free_prompts();
         return bail(cuda_fail(e, "prompt upload"));
       }
-      if ((rc = prefill_device(*m, *c, d, len, row, phase))) {
+      // wide sessions: logits row 0 of the GEMV workspace, then into the wide logits
+      if ((rc = prefill_device(*m, *c, d, len, wide ? 0 : row, phase))) {
         free_prompts();
         return bail(rc);
+      }
+      if (wide) {
+        const size_t vb = (size_t)m->g.vocab * 4;
+        cudaError_t ce = cudaMemcpyAsync(m->wide_logits + (size_t)row * m->g.vocab, m->logits, vb,
+                                         cudaMemcpyDeviceToDevice, m->stream);
+        if (ce != cudaSuccess) {
+          free_prompts();
+          return bail(cuda_fail(ce, "prefill logits"));
+        }
       }
       (side ? ss->uncond_row : ss->cond_row).push_back(row);
       ++row;
@@ -388,8 +402,16 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
     rows[r].active = 1;
     rows[r].advance = 1;
   }
-  if ((rc = upload_rows(*m, rows))) return bail(rc);
-  ss->sp = make_params(*m, ss->bufs, ss->cfg, V, m->logits, V);
+  if (wide) {
+    if ((e = cudaMemcpyAsync(m->wide_rows, rows.data(), R * sizeof(DevRow), cudaMemcpyHostToDevice, m->stream)) !=
+        cudaSuccess)
+      return bail(cuda_fail(e, "row descriptors"));
+    ss->sp = make_params(*m, ss->bufs, ss->cfg, V, m->wide_logits, V);
+    ss->sp.rows = m->wide_rows;
+  } else {
+    if ((rc = upload_rows(*m, rows))) return bail(rc);
+    ss->sp = make_params(*m, ss->bufs, ss->cfg, V, m->logits, V);
+  }
 
   // ---- step 0: the first token comes from the prefill logits (sampling.rs:260-267)
   if (draw && (e = launch_mt_words(m->stream, ss->bufs.mt, ss->bufs.words, 2 * V, ss->bufs.reqs, (int)n)))
@@ -398,7 +420,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
 
   // ---- decode step graph: forward(R rows) || MT words, then sample
   if (s->max_tokens > 1) {
-    if ((rc = prepare_step_plan(*m, R, phase))) return bail(rc);
+    if (!wide && (rc = prepare_step_plan(*m, R, phase))) return bail(rc);
     cudaGraph_t graph;
     if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
       return bail(cuda_fail(e, "capture"));
@@ -409,10 +431,21 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
       if (ce == cudaSuccess) ce = launch_mt_words(m->side, ss->bufs.mt, ss->bufs.words, 2 * V, ss->bufs.reqs, (int)n);
       if (ce == cudaSuccess) ce = cudaEventRecord(m->ev_join, m->side);
     }
-    if (ce == cudaSuccess) ce = encode_forward(*m, m->stream, R, true, phase, ss->bufs.flags + 1);
+    int wrc = 0;
+    if (ce == cudaSuccess) {
+      if (wide) {
+        if ((wrc = encode_forward_wide(*m, m->stream, R, phase))) ce = cudaErrorUnknown;
+      } else {
+        ce = encode_forward(*m, m->stream, R, true, phase, ss->bufs.flags + 1);
+      }
+    }
     if (ce == cudaSuccess && draw) ce = cudaStreamWaitEvent(m->stream, m->ev_join, 0);
     if (ce == cudaSuccess) ce = launch_sample(m->stream, false, ss->sp, (int)n);
     e = cudaStreamEndCapture(m->stream, &graph);
+    if (wrc) {
+      if (e == cudaSuccess) cudaGraphDestroy(graph);
+      return bail(wrc);
+    }
     if (ce != cudaSuccess) return bail(cuda_fail(ce, "decode step capture"));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaStreamEndCapture"));
     e = cudaGraphInstantiate(&ss->graph, graph, 0);
@@ -433,7 +466,9 @@ void* yue2_session_stream(Yue2Session* ss) { return ss ? (void*)ss->m->stream : 
 
 uint64_t yue2_session_kernels_per_step(const Yue2Session* ss) {
   if (!ss) return 0;
-  return (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R) + (ss->s.temperature != 0.f ? 1 : 0) + 2;
+  const uint64_t forward = ss->wide ? (uint64_t)wide_kernels_per_step(*ss->m, ss->phase)
+                                    : (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R);
+  return forward + (ss->s.temperature != 0.f ? 1 : 0) + 2;
 }
 
 int yue2_session_step(Yue2Session* ss, uint64_t steps, uint64_t* launched) {

@@ -1,5 +1,6 @@
-// Prompt prefill as tensor-core GEMMs (Model::prefill_phase, src/model.rs:508-522, whose
-// layer math is Model::hidden's, src/model.rs:523-591).
+// Forward passes over many rows as tensor-core GEMMs: prompt prefill chunks
+// (Model::prefill_phase, src/model.rs:508-522) and decode steps of more than kMaxRows rows
+// (many songs per GPU; Model::hidden's decode branch, src/model.rs:523-591, per row).
 //
 // A prompt of n >= kPrefillGemmMin ids is cut into equal chunks of at most
 // m.prefill_chunk (<= kPrefillRows) consecutive positions of one cache. Each chunk goes
@@ -14,6 +15,10 @@
 //                          the tensor cores (kernels_prefill_attn.cu); head sizes it does
 //                          not take (and YUE2_CUDA_PREFILL_ATTN=rows) use attn_kernel per row
 // The last row's hidden state goes through the LM head GEMV when logits are wanted.
+//
+// A wide decode step runs the same layer sequence over R rows of distinct caches, with
+// the decode attention kernel (QK norm, RoPE and the KV append fused in, one query per
+// row), then the final norm and the LM head as one more GEMM (bf16 logits widened to f32).
 #include <cublasLt.h>
 #include <cuda_runtime.h>
 
@@ -206,8 +211,10 @@ static int ensure_prefill(Yue2Model& m) {
 }
 
 // Y[C, N] (row stride ldy) = X[C, K] (row stride ldx) . W[N, K]^T, bf16 in and out, f32
-// accumulation. Algorithms that split K are excluded, so a row's result depends only on
-// the shapes (no cross-CTA reduction order).
+// accumulation. Algorithms may split K only with an out-of-place f32 reduction in a
+// separate pass (YUE2_CUDA_GEMM_SPLITK=1; default: no split), never with in-place or
+// output-type partial sums, so a row's result depends only on the shapes and repeats
+// bit for bit.
 static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
                      int C) {
   PrefillBufs& P = *m.prefill;
@@ -225,7 +232,8 @@ static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16
         (st = cublasLtMatrixLayoutCreate(&gm.d, CUDA_R_16BF, N, C, ldy)))
       return lt_fail(st, "cuBLASLt descriptor");
     cublasLtMatmulPreference_t pref = nullptr;
-    const uint32_t no_split = CUBLASLT_REDUCTION_SCHEME_NONE;
+    const uint32_t no_split = m.gemm_split_k ? (uint32_t)CUBLASLT_REDUCTION_SCHEME_COMPUTE_TYPE
+                                             : (uint32_t)CUBLASLT_REDUCTION_SCHEME_NONE;
     cublasLtMatmulHeuristicResult_t res{};
     int found = 0;
     if ((st = cublasLtMatmulPreferenceCreate(&pref)) ||
@@ -276,13 +284,14 @@ static cudaError_t launch_residual_norm(cudaStream_t s, float* x, const uint16_t
   return launch_with(s, false, dim3(C), dim3(256), 0, (const void*)residual_norm_kernel<256>, args);
 }
 
-// Per-row split-K decode attention over the chunk's rows (head sizes the tensor-core
-// kernel does not take).
-static int row_attention(Yue2Model& m, PrefillBufs& P, int l, int C, int splits) {
+// Split-K decode attention with one query per row: decode rows (fused: QK norm, RoPE and
+// the row's K/V append in the kernel) or prefill chunk rows whose K/V rope_append wrote
+// (head sizes the tensor-core prefill kernel does not take).
+static int row_attention(Yue2Model& m, PrefillBufs& P, DevRow* rows, int l, int R, int splits, bool fused) {
   const LayerW& w = m.layers[l];
   const Geometry& g = m.g;
   AttnParams ap = {};
-  ap.rows = P.rows;
+  ap.rows = rows;
   ap.q = P.q;
   ap.out = P.attn;
   ap.part = P.part;
@@ -291,7 +300,7 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, int l, int C, int splits)
   ap.layer = l;
   ap.splits = splits;
   ap.scale = 1.0f / sqrtf((float)g.dim);
-  ap.fused = 0;
+  ap.fused = fused ? 1 : 0;
   ap.qkv = P.qkv;
   ap.q_norm = w.q_norm;
   ap.k_norm = w.k_norm;
@@ -299,18 +308,89 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, int l, int C, int splits)
   ap.sin_tab = m.sin_tab;
   ap.max_pos = m.max_pos;
   ap.error = m.flags + 1;
-  CK(launch_attention(m.stream, false, ap, C));
+  CK(launch_attention(m.stream, false, ap, R));
   return 0;
 }
 
-// ------------------------------------------------------------------ one chunk, all layers
-static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t L0, uint64_t n, uint64_t start,
-                         int C) {
+// ------------------------------------------------------------------ the layers over R rows
+// Layers of R rows whose embeddings are in P.x (f32), ending with the last residual added
+// (the final norm is the caller's). Prefill chunk rows (decode = false) belong to one
+// cache at positions pos0 + r: rope_append writes all their K/V, then the causal prefill
+// attention runs. Decode rows (decode = true) each have their own cache: the decode
+// attention kernel applies the QK norm and RoPE and appends each row's K/V itself.
+static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const uint64_t* pages, int pos0) {
   PrefillBufs& P = *m.prefill;
   const Geometry& g = m.g;
   const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
   cudaStream_t s = m.stream;
   int rc;
+  // one wave of attention CTAs where R is small; the partials hold cap rows x kvh
+  const int splits = std::max(1, std::min(std::min(m.max_splits, P.cap / R), 2 * m.sms / (g.kvh * R)));
+  for (int l = 0; l < g.layers; ++l) {
+    const LayerW& w = m.layers[l];
+    CK(launch_residual_norm(s, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, R));
+    {
+      const uint16_t* W[3] = {w.q, w.k, w.v};
+      const int N[3] = {qd, kd, kd};
+      if ((rc = gemm_concat(m, W, N, 3, H, P.xb, H, P.qkv, qd + 2 * kd, R))) return rc;
+    }
+    if (decode) {
+      if ((rc = row_attention(m, P, rows, l, R, splits, true))) return rc;
+    } else {
+      RopeParams rp = {};
+      rp.rows = rows;
+      rp.qkv = P.qkv;
+      rp.q_out = P.q;
+      rp.cos_tab = m.cos_tab;
+      rp.sin_tab = m.sin_tab;
+      rp.q_norm = w.q_norm;
+      rp.k_norm = w.k_norm;
+      rp.g = g;
+      rp.layer = l;
+      rp.max_pos = m.max_pos;
+      rp.error = m.flags + 1;
+      CK(launch_rope_append(s, false, rp, R));
+      if (m.prefill_tc_attn && prefill_attention_supported(g)) {
+        PrefillAttnParams fp = {};
+        fp.pages = pages;
+        fp.q = P.q;
+        fp.out = P.attn;
+        fp.g = g;
+        fp.layer = l;
+        fp.C = R;
+        fp.pos0 = pos0;
+        fp.scale = 1.0f / sqrtf((float)g.dim);
+        CK(launch_prefill_attention(s, fp));
+      } else if ((rc = row_attention(m, P, rows, l, R, splits, false))) {
+        return rc;
+      }
+    }
+    if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, R))) return rc;
+    CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, R));
+    {
+      const uint16_t* W[2] = {w.gate, w.up};
+      const int N[2] = {I, I};
+      if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, R))) return rc;
+    }
+    {
+      const uint16_t* gu = P.gu;
+      uint16_t* h = P.h;
+      int inter = I, nrows = R;
+      void* args[] = {&gu, &inter, &nrows, &h};
+      const int blocks = std::min(4 * m.sms, (int)(((size_t)R * (I / 8) + 255) / 256));
+      CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)swiglu_kernel, args));
+    }
+    if ((rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, R))) return rc;
+  }
+  return 0;
+}
+
+// ------------------------------------------------------------------ one prefill chunk
+static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t L0, uint64_t n, uint64_t start,
+                         int C) {
+  PrefillBufs& P = *m.prefill;
+  const Geometry& g = m.g;
+  cudaStream_t s = m.stream;
   {
     DevRow* rows = P.rows;
     const uint64_t* pages = c.d_pages;
@@ -318,65 +398,93 @@ static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint6
     void* args[] = {&rows, &C, &pages, &d_ids, &pb, &pe, &p0};
     CK(launch_with(s, false, dim3((C + 127) / 128), dim3(128), 0, (const void*)prefill_rows_kernel, args));
   }
-  CK(launch_embed(s, false, P.rows, C, m.embed, H, g.vocab, P.x, m.flags + 0));
-  // one wave of attention CTAs where the chunk is short; the partials hold cap rows x kvh
-  const int splits = std::max(1, std::min(std::min(m.max_splits, P.cap / C), 2 * m.sms / (g.kvh * C)));
-  for (int l = 0; l < g.layers; ++l) {
-    const LayerW& w = m.layers[l];
-    CK(launch_residual_norm(s, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, C));
-    {
-      const uint16_t* W[3] = {w.q, w.k, w.v};
-      const int N[3] = {qd, kd, kd};
-      if ((rc = gemm_concat(m, W, N, 3, H, P.xb, H, P.qkv, qd + 2 * kd, C))) return rc;
-    }
-    RopeParams rp = {};
-    rp.rows = P.rows;
-    rp.qkv = P.qkv;
-    rp.q_out = P.q;
-    rp.cos_tab = m.cos_tab;
-    rp.sin_tab = m.sin_tab;
-    rp.q_norm = w.q_norm;
-    rp.k_norm = w.k_norm;
-    rp.g = g;
-    rp.layer = l;
-    rp.max_pos = m.max_pos;
-    rp.error = m.flags + 1;
-    CK(launch_rope_append(s, false, rp, C));
-    if (m.prefill_tc_attn && prefill_attention_supported(g)) {
-      PrefillAttnParams fp = {};
-      fp.pages = c.d_pages;
-      fp.q = P.q;
-      fp.out = P.attn;
-      fp.g = g;
-      fp.layer = l;
-      fp.C = C;
-      fp.pos0 = (int)(L0 + start);
-      fp.scale = 1.0f / sqrtf((float)g.dim);
-      CK(launch_prefill_attention(s, fp));
-    } else if ((rc = row_attention(m, P, l, C, splits))) {
-      return rc;
-    }
-    if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, C))) return rc;
-    CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, C));
-    {
-      const uint16_t* W[2] = {w.gate, w.up};
-      const int N[2] = {I, I};
-      if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, C))) return rc;
-    }
-    {
-      const uint16_t* gu = P.gu;
-      uint16_t* h = P.h;
-      int inter = I, rows = C;
-      void* args[] = {&gu, &inter, &rows, &h};
-      const int blocks = std::min(4 * m.sms, (int)(((size_t)C * (I / 8) + 255) / 256));
-      CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)swiglu_kernel, args));
-    }
-    if ((rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, C))) return rc;
-  }
+  CK(launch_embed(s, false, P.rows, C, m.embed, g.hidden, g.vocab, P.x, m.flags + 0));
+  const int rc = encode_layers(m, P.rows, C, false, c.d_pages, (int)(L0 + start));
+  if (rc) return rc;
   // the last layer's residual (the LM head applies the final norm itself)
-  CK(launch_residual_norm(s, P.x, P.y, nullptr, H, g.eps, nullptr, C));
+  CK(launch_residual_norm(s, P.x, P.y, nullptr, g.hidden, g.eps, nullptr, C));
   return 0;
 }
+
+// ------------------------------------------------------------------ wide decode steps
+// LM head rows [lo, hi) cover the phase's window and its stop row (project_phase,
+// src/model.rs:478-507): the whole vocabulary, the codec window with MUSIC_END just below
+// it, or the Abc window up to and including ABC_END (the 205 ids between are computed
+// and dropped).
+static void head_span(const Yue2Model& m, int phase, int& lo, int& hi, int& start, int& end, int& stop) {
+  const int V = m.g.vocab;
+  if (phase == kPhaseVocab) {
+    lo = start = 0;
+    hi = end = V;
+    stop = -1;
+    return;
+  }
+  start = phase == kPhaseAbc ? 0 : (int)kCodecOffset;
+  end = phase == kPhaseAbc ? (int)kEOD : (int)(kCodecOffset + kCodecSize);
+  stop = phase == kPhaseAbc ? (int)kAbcEnd : (int)kMusicEnd;
+  lo = std::min(start, stop);
+  hi = std::max(end, stop + 1);
+}
+
+// logits[r][id] = bf16 head output h[r][id - lo] for ids of the window and the stop row
+// (the rest of the row is already -inf outside the full-vocabulary phase).
+__global__ void head_scatter_kernel(const uint16_t* __restrict__ h, int ldh, int R, int lo, int n, int start, int end,
+                                    int stop, float* __restrict__ logits, int V) {
+  const size_t total = (size_t)R * n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / n), j = (int)(i - (size_t)r * n), id = lo + j;
+    if ((id >= start && id < end) || id == stop) logits[(size_t)r * V + id] = bf2f(h[(size_t)r * ldh + j]);
+  }
+}
+
+int ensure_wide(Yue2Model& m) {
+  int rc = ensure_prefill(m);
+  if (rc || m.wide_rows) return rc;
+  const size_t V = m.g.vocab;
+  void *a = nullptr, *b = nullptr, *c = nullptr;
+  if ((rc = m.alloc(&a, kMaxWideRows * sizeof(DevRow))) || (rc = m.alloc(&b, kMaxWideRows * V * 4)) ||
+      (rc = m.alloc(&c, kMaxWideRows * ((V + 7) & ~(size_t)7) * 2)))
+    return rc;
+  CK(cudaMemset(a, 0, kMaxWideRows * sizeof(DevRow)));
+  m.wide_rows = (DevRow*)a;
+  m.wide_logits = (float*)b;
+  m.wide_head = (uint16_t*)c;
+  return 0;
+}
+
+// One decode step of R (kMaxRows < R <= kMaxWideRows) rows in m.wide_rows: embed, layers,
+// final norm, LM head into m.wide_logits, positions advanced.
+int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase) {
+  if (s != m.stream) return fail(YUE2_ERR_INVALID, "wide decode steps run on the model's stream");
+  int rc = ensure_wide(m);
+  if (rc) return rc;
+  PrefillBufs& P = *m.prefill;
+  const Geometry& g = m.g;
+  const int H = g.hidden, V = g.vocab;
+  CK(launch_embed(s, false, m.wide_rows, R, m.embed, H, V, P.x, m.flags + 0));
+  if ((rc = encode_layers(m, m.wide_rows, R, true, nullptr, 0))) return rc;
+  CK(launch_residual_norm(s, P.x, P.y, m.final_norm, H, g.eps, P.xb, R));
+  int lo, hi, start, end, stop;
+  head_span(m, phase, lo, hi, start, end, stop);
+  const int n = hi - lo, ldh = (n + 7) & ~7;
+  if (phase != kPhaseVocab) CK(launch_fill_f32(s, m.wide_logits, (size_t)R * V, -INFINITY));
+  if ((rc = gemm_bf16(m, m.lm_head + (size_t)lo * H, n, H, P.xb, H, m.wide_head, ldh, R))) return rc;
+  {
+    const uint16_t* h = m.wide_head;
+    float* logits = m.wide_logits;
+    int ld = ldh, rows = R, vocab = V;
+    void* args[] = {&h, &ld, &rows, &lo, (void*)&n, &start, &end, &stop, &logits, &vocab};
+    const int blocks = std::min(8 * m.sms, (int)(((size_t)R * n + 255) / 256));
+    CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)head_scatter_kernel, args));
+  }
+  CK(launch_step_end(s, false, m.wide_rows, R));
+  return 0;
+}
+
+// Kernels of this library per wide step (the cuBLASLt GEMMs not counted): embed, per layer
+// two norms, attention and SwiGLU, the final norm, [the -inf fill], the head scatter and
+// step_end.
+int wide_kernels_per_step(const Yue2Model& m, int phase) { return 1 + 4 * m.g.layers + 1 + (phase != kPhaseVocab) + 2; }
 
 int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
   const Geometry& g = m.g;

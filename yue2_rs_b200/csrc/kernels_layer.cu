@@ -442,21 +442,35 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   attn_item<D, G, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
 }
 
-// The reservation is at least 77 KB, so that no SM holds more than two attention CTAs: the
-// block scheduler would otherwise stack three on the SMs that free up first and leave
-// others idle.
-int attention_smem_bytes(int dim, int groups) {
-  const int tiles = 2 * 4 * 32 * dim * 2;
+// Passes of more than kMaxRows rows: the pipelined tile loop.
+template <int D, int G>
+__global__ void __launch_bounds__(128) attn_pipe_kernel(const AttnParams a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  attn_item<D, G, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+}
+
+static int attention_smem_need(int dim, int groups, bool pipe = false) {
+  const int tiles = (pipe ? 3 : 2) * 4 * 32 * dim * 2;
   const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4;
   const int merge = 4 * groups * dim * 4;
-  const int need = (tiles > merge ? tiles : merge) + extra;
+  return (tiles > merge ? tiles : merge) + extra;
+}
+
+// The reservation of a one-wave launch is at least 77 KB, so that no SM holds more than two
+// attention CTAs: the block scheduler would otherwise stack three on the SMs that free up
+// first and leave others idle.
+int attention_smem_bytes(int dim, int groups) {
+  const int need = attention_smem_need(dim, groups);
   return need > 77 * 1024 ? need : 77 * 1024;
 }
 
+// Passes of more than kMaxRows rows launch many waves of CTAs, each streaming many tiles
+// per warp: they use the pipelined loop (96 KB at dim 128, two CTAs per SM).
 template <int D, int G>
 static cudaError_t attn_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
-  const void* fn = (const void*)attn_kernel<D, G>;
-  const int smem = attention_smem_bytes(D, G);
+  const bool pipe = R > kMaxRows;
+  const void* fn = pipe ? (const void*)attn_pipe_kernel<D, G> : (const void*)attn_kernel<D, G>;
+  const int smem = pipe ? attention_smem_need(D, G, true) : attention_smem_bytes(D, G);
   cudaError_t e = ensure_smem_attr(fn, smem);
   if (e != cudaSuccess || g_configure_only) return e;
   AttnParams copy = p;
@@ -508,6 +522,7 @@ cudaError_t prepare_kernels() {
       a.g.kvh = 1;
       a.g.heads = G;
       if (e == cudaSuccess) e = launch_attention(nullptr, false, a, 1);
+      if (e == cudaSuccess) e = launch_attention(nullptr, false, a, kMaxRows + 1);  // pipelined form
     }
   g_configure_only = false;
   return e;
@@ -522,8 +537,9 @@ __global__ void step_end_kernel(DevRow* rows, int R) {
 }
 
 cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R) {
+  if (R < 1 || R > 1024) return cudaErrorInvalidValue;
   void* args[] = {&rows, &R};
-  return launch_with(s, pdl, dim3(1), dim3(32), 0, (const void*)step_end_kernel, args);
+  return launch_with(s, pdl, dim3(1), dim3((R + 31) / 32 * 32), 0, (const void*)step_end_kernel, args);
 }
 
 // ------------------------------------------------------------------ synthetic data

@@ -151,7 +151,8 @@ class Model:
         return Cache(self, capacity)
 
     def forward_rows(self, caches, ids, phase=Phase.VOCAB):
-        """One new id for each of up to 16 distinct caches in one weight pass; logits [rows, vocab]."""
+        """One new id for each of up to 256 distinct caches in one pass (GEMV up to 16 rows, GEMMs
+        beyond); logits [rows, vocab]."""
         n = len(caches)
         arr = (ctypes.c_void_p * n)(*[c._h for c in caches])
         ids = np.ascontiguousarray(ids, dtype=np.int64)
