@@ -104,7 +104,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   // the tile holding the new position is written in this launch (fused) or by the
   // preceding kernel (prefill rows): it is never fetched before the wait
   const int first_tile = t0 + warp;
-  const bool early = !PIPE && STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  const bool early = STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
   // PIPE: K (swizzled) of tile t into buffer buf, V of tile t; one commit group each
   auto stage_k = [&](int t, int buf) {
     const int key0 = t << 5;
@@ -129,7 +129,14 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
     cp_async_commit();
   };
-  if (early) stage(first_tile);
+  if (early) {
+    if constexpr (PIPE) {
+      stage_k(first_tile, 0);
+      stage_v(first_tile);
+    } else {
+      stage(first_tile);
+    }
+  }
 
   if (STANDALONE) {
     pdl_wait();
@@ -183,7 +190,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   }
   float* pw = ps + warp * G * 32;
 
-  if (PIPE && first_tile < t1) {
+  if (PIPE && first_tile < t1 && !early) {
     stage_k(first_tile, 0);
     stage_v(first_tile);
   }

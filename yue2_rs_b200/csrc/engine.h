@@ -45,6 +45,7 @@ struct Yue2Model {
   int gemv_grid = 148;
   bool use_pdl = true, use_graphs = true;
   bool use_step = false;  // persistent decode-step kernel for R <= 2 (YUE2_CUDA_STEP=1)
+  int ctx_hint = 0;       // longest row context of the next captured forward (picks the attention loop)
   struct StepPlan {
     y2::StepGemv* phases = nullptr;
     y2::AttnParams* attn = nullptr;
@@ -132,6 +133,7 @@ cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R
 cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float* x, int R, int dst_row, int phase,
                              const int32_t* skip);
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
+int attn_pipe_for(const Yue2Model& m, int R);
 int prepare_step_plan(Yue2Model& m, int R, int phase);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);

@@ -88,6 +88,7 @@ struct AttnParams {
   const float *q_norm, *k_norm, *cos_tab, *sin_tab;
   int max_pos;
   int32_t* error;
+  int pipe;  // 1: the pipelined tile loop (long contexts); passes of > kMaxRows rows always use it
 };
 
 // Causal attention of a prefill chunk: rows [0, C) at positions pos0 + row of one cache,

@@ -6,6 +6,7 @@
 // decode attention (src/model.rs:314-397, src/attention.metal:206-317).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -464,11 +465,22 @@ int attention_smem_bytes(int dim, int groups) {
   return need > 77 * 1024 ? need : 77 * 1024;
 }
 
-// Passes of more than kMaxRows rows launch many waves of CTAs, each streaming many tiles
-// per warp: they use the pipelined loop (96 KB at dim 128, two CTAs per SM).
+// The pipelined tile loop (96 KB at dim 128, two CTAs per SM): always for passes of more
+// than kMaxRows rows, which launch many waves of CTAs streaming many tiles per warp;
+// for the others when the caller asks (p.pipe: long contexts). YUE2_CUDA_ATTN_PIPE=1 / 0
+// forces it on / off everywhere.
+static int attn_pipe_mode() {
+  static int mode = [] {
+    const char* v = getenv("YUE2_CUDA_ATTN_PIPE");
+    return v && *v ? atoi(v) : -1;
+  }();
+  return mode;
+}
+
 template <int D, int G>
 static cudaError_t attn_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
-  const bool pipe = R > kMaxRows;
+  const int mode = attn_pipe_mode();
+  const bool pipe = mode == 1 || (mode != 0 && (R > kMaxRows || p.pipe));
   const void* fn = pipe ? (const void*)attn_pipe_kernel<D, G> : (const void*)attn_kernel<D, G>;
   const int smem = pipe ? attention_smem_need(D, G, true) : attention_smem_bytes(D, G);
   cudaError_t e = ensure_smem_attr(fn, smem);
