@@ -54,8 +54,13 @@ Y2_DEV void attn_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // after another one (attn_merge_slice). PIPE (passes of many rows, each CTA streaming
 // many tiles per warp): two K buffers per warp; the next tile's K is requested before the
 // current tile's scores and its V right after the current P.V, so loads overlap compute.
-template <int D, int G, bool STANDALONE, bool PIPE = false>
+// MMA (implies PIPE; G <= 8, D <= 128): scores and P.V on the tensor cores. The G query
+// heads are the rows of one m16n8k16 A tile (bf16; q is already bf16-exact), a 32-key K
+// tile gives four n-tiles, and P.V multiplies P split into bf16 hi + lo parts so that the
+// probabilities keep f32 accuracy. V rows past the last key are zero-filled.
+template <int D, int G, bool STANDALONE, bool PIPE = false, bool MMA = false>
 Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned char* smem_raw) {
+  static_assert(!MMA || (PIPE && G <= 8 && D <= 128), "tensor-core attention shape");
   constexpr int CPR = D / 8;  // 16-byte chunks per key row
   constexpr int DL = D / 32;  // dims per lane
   constexpr int NW = 4;
@@ -125,7 +130,11 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
     for (int i = lane; i < 32 * CPR; i += 32) {
       const int j = i / CPR, c = i % CPR;
-      if (j < nk) cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+      if constexpr (MMA) {  // swizzled for ldmatrix.trans; rows past the last key zeroed
+        cp_async16_zfill(vt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, vb + (size_t)(j < nk ? j : 0) * D + c * 8, j < nk);
+      } else if (j < nk) {
+        cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+      }
     }
     cp_async_commit();
   };
@@ -180,126 +189,249 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   }
   attn_sync();
 
-  float m[G], l[G], acc[G][DL];
+  float* wacc = reinterpret_cast<float*>(smem_raw);  // [NW][G][D] f32 after the loops
+  if constexpr (MMA) {
+    constexpr int KS = D / 16, NT = D / 8;
+    auto sw = [](int rr, int c) { return (uint32_t)(rr * D * 2 + ((c ^ (rr & 7)) << 4)); };
+    unsigned char* qsb = reinterpret_cast<unsigned char*>(wbuf_all + NW * D);  // [16][D] bf16
+    for (int i = threadIdx.x; i < 16 * CPR; i += 128) {
+      const int rr = i / CPR, c = i % CPR;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (rr < G) {
+        const float* src = qs + rr * D + c * 8;
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
-  }
-  float* pw = ps + warp * G * 32;
-
-  if (PIPE && first_tile < t1 && !early) {
-    stage_k(first_tile, 0);
-    stage_v(first_tile);
-  }
-  for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
-    const int key0 = t << 5;
-    const int nk = min(32, keys - key0);
-    const uint16_t* kcur = kt + (PIPE ? (size_t)(it & 1) * 32 * D : 0);
-    if constexpr (PIPE) {
-      if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
-      else cp_async_commit();  // keeps the group count: K(t) is third from the end
-      cp_async_wait<2>();
-    } else {
-      if (!(early && t == first_tile)) stage(t);
-      cp_async_wait<0>();
+        for (int k = 0; k < 4; ++k) w[k] = pack_bf16x2(src[2 * k], src[2 * k + 1]);
+      }
+      *reinterpret_cast<uint4*>(qsb + sw(rr, c)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    __syncwarp();
-
-    float sc[G];
+    attn_sync();
+    const int g8 = lane >> 2, t4 = lane & 3;
+    uint32_t qf[KS][2];  // A fragments a0, a2 (head rows 0-7); rows 8-15 are zero
 #pragma unroll
-    for (int h = 0; h < G; ++h) sc[h] = 0.f;
-    if (lane < nk) {
-#pragma unroll 4
-      for (int c = 0; c < CPR; ++c) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(kcur + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
-        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
-        const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t tq[4];
+      const int mi = lane >> 3, rr = (mi & 1) * 8 + (lane & 7);
+      ldsm_x4(tq, qsb + sw(rr, 2 * kk + (mi >> 1)));
+      qf[kk][0] = tq[0];
+      qf[kk][1] = tq[2];
+    }
+    float o[NT][4];
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + c * 8);
-          const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + c * 8 + 4);
-          float s = sc[h];
-          s = fmaf(qa.x, k0, s);
-          s = fmaf(qa.y, k1, s);
-          s = fmaf(qa.z, k2, s);
-          s = fmaf(qa.w, k3, s);
-          s = fmaf(qb.x, k4, s);
-          s = fmaf(qb.y, k5, s);
-          s = fmaf(qb.z, k6, s);
-          s = fmaf(qb.w, k7, s);
-          sc[h] = s;
+    for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float mrow = -INFINITY, lrow = 0.f;  // head g8
+    if (first_tile < t1 && !early) {
+      stage_k(first_tile, 0);
+      stage_v(first_tile);
+    }
+    for (int t = first_tile, it = 0; t < t1; t += NW, ++it) {
+      const int nk = min(32, keys - (t << 5));
+      const unsigned char* kb = reinterpret_cast<const unsigned char*>(kt + (size_t)(it & 1) * 32 * D);
+      const unsigned char* vb = reinterpret_cast<const unsigned char*>(vt);
+      if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
+      else cp_async_commit();
+      cp_async_wait<2>();
+      __syncwarp();
+      float s[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < KS; kk += 2) {
+          uint32_t b[4];
+          ldsm_x4(b, kb + sw(8 * j + (lane & 7), 2 * kk + (lane >> 3)));
+          mma_bf16_16816(s[j], qf[kk][0], 0u, qf[kk][1], 0u, b[0], b[1]);
+          mma_bf16_16816(s[j], qf[kk + 1][0], 0u, qf[kk + 1][1], 0u, b[2], b[3]);
         }
       }
-    }
+      float mx = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
-      const float mnew = fmaxf(m[h], warp_max(s));
-      const float alpha = m[h] == -INFINITY ? 0.f : __expf(m[h] - mnew);
-      const float pv = lane < nk ? __expf(s - mnew) : 0.f;
-      l[h] = l[h] * alpha + warp_sum(pv);
-      m[h] = mnew;
-      pw[h * 32 + lane] = pv;
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
-    }
-    if constexpr (PIPE) cp_async_wait<1>();  // V(t); K of the next tile may stay in flight
-    __syncwarp();
-    for (int j = 0; j < nk; ++j) {
-      const uint16_t* vr = vt + (size_t)j * D + lane * DL;
-      float vv[DL];
-      if constexpr (DL == 2) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
-        vv[0] = bf_lo(w);
-        vv[1] = bf_hi(w);
-      } else if constexpr (DL == 4) {
-        const uint2 w = *reinterpret_cast<const uint2*>(vr);
-        vv[0] = bf_lo(w.x);
-        vv[1] = bf_hi(w.x);
-        vv[2] = bf_lo(w.y);
-        vv[3] = bf_hi(w.y);
-      } else {
-        const uint4 w = *reinterpret_cast<const uint4*>(vr);
-        vv[0] = bf_lo(w.x);
-        vv[1] = bf_hi(w.x);
-        vv[2] = bf_lo(w.y);
-        vv[3] = bf_hi(w.y);
-        vv[4] = bf_lo(w.z);
-        vv[5] = bf_hi(w.z);
-        vv[6] = bf_lo(w.w);
-        vv[7] = bf_hi(w.w);
+        for (int e = 0; e < 2; ++e) {
+          const float v = 8 * j + 2 * t4 + e < nk ? s[j][e] * a.scale : -INFINITY;
+          s[j][e] = v;
+          mx = fmaxf(mx, v);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(mrow, mx);  // key 0 of the tile is always valid: finite
+      const float al = mrow == -INFINITY ? 0.f : __expf(mrow - mn);
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float p = __expf(s[j][e] - mn);
+          s[j][e] = p;
+          sum += p;
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      lrow = lrow * al + sum;
+      mrow = mn;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        o[j][0] *= al;
+        o[j][1] *= al;
       }
+      cp_async_wait<1>();  // V(t); K of the next tile may stay in flight
+      __syncwarp();
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float pj = pw[h * 32 + j];
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t h0 = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+        const uint32_t h2 = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        const uint32_t l0 = pack_bf16x2(s[2 * kk][0] - bf_lo(h0), s[2 * kk][1] - bf_hi(h0));
+        const uint32_t l2 = pack_bf16x2(s[2 * kk + 1][0] - bf_lo(h2), s[2 * kk + 1][1] - bf_hi(h2));
 #pragma unroll
-        for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
+        for (int jd = 0; jd < NT; jd += 2) {
+          uint32_t b[4];
+          const int mi = lane >> 3;
+          ldsm_x4_trans(b, vb + sw(16 * kk + (mi & 1) * 8 + (lane & 7), jd + (mi >> 1)));
+          mma_bf16_16816(o[jd], h0, 0u, h2, 0u, b[0], b[1]);
+          mma_bf16_16816(o[jd], l0, 0u, l2, 0u, b[0], b[1]);
+          mma_bf16_16816(o[jd + 1], h0, 0u, h2, 0u, b[2], b[3]);
+          mma_bf16_16816(o[jd + 1], l0, 0u, l2, 0u, b[2], b[3]);
+        }
       }
-    }
-    __syncwarp();
-    if constexpr (PIPE) {
+      __syncwarp();
       if (t + NW < t1) stage_v(t + NW);
       else cp_async_commit();
     }
-  }
-  if constexpr (PIPE) cp_async_wait<0>();
-
-  // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
-  attn_sync();
-  float* wacc = reinterpret_cast<float*>(smem_raw);
-  if (lane == 0)
+    cp_async_wait<0>();
+    // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
+    attn_sync();
+    if (g8 < G) {
+      if (t4 == 0) {
+        wm[warp * G + g8] = mrow;
+        wl[warp * G + g8] = lrow;
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        wacc[((size_t)warp * G + g8) * D + 8 * j + 2 * t4] = o[j][0];
+        wacc[((size_t)warp * G + g8) * D + 8 * j + 2 * t4 + 1] = o[j][1];
+      }
+    }
+  } else {
+    float m[G], l[G], acc[G][DL];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      wm[warp * G + h] = m[h];
-      wl[warp * G + h] = l[h];
+      m[h] = -INFINITY;
+      l[h] = 0.f;
+#pragma unroll
+      for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
     }
+    float* pw = ps + warp * G * 32;
+
+    if (PIPE && first_tile < t1 && !early) {
+      stage_k(first_tile, 0);
+      stage_v(first_tile);
+    }
+    for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
+      const int key0 = t << 5;
+      const int nk = min(32, keys - key0);
+      const uint16_t* kcur = kt + (PIPE ? (size_t)(it & 1) * 32 * D : 0);
+      if constexpr (PIPE) {
+        if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
+        else cp_async_commit();  // keeps the group count: K(t) is third from the end
+        cp_async_wait<2>();
+      } else {
+        if (!(early && t == first_tile)) stage(t);
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+
+      float sc[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h)
+      for (int h = 0; h < G; ++h) sc[h] = 0.f;
+      if (lane < nk) {
+#pragma unroll 4
+        for (int c = 0; c < CPR; ++c) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(kcur + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
+          const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+          const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
 #pragma unroll
-    for (int e = 0; e < DL; ++e) wacc[((size_t)warp * G + h) * D + lane * DL + e] = acc[h][e];
+          for (int h = 0; h < G; ++h) {
+            const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + c * 8);
+            const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + c * 8 + 4);
+            float s = sc[h];
+            s = fmaf(qa.x, k0, s);
+            s = fmaf(qa.y, k1, s);
+            s = fmaf(qa.z, k2, s);
+            s = fmaf(qa.w, k3, s);
+            s = fmaf(qb.x, k4, s);
+            s = fmaf(qb.y, k5, s);
+            s = fmaf(qb.z, k6, s);
+            s = fmaf(qb.w, k7, s);
+            sc[h] = s;
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
+        const float mnew = fmaxf(m[h], warp_max(s));
+        const float alpha = m[h] == -INFINITY ? 0.f : __expf(m[h] - mnew);
+        const float pv = lane < nk ? __expf(s - mnew) : 0.f;
+        l[h] = l[h] * alpha + warp_sum(pv);
+        m[h] = mnew;
+        pw[h * 32 + lane] = pv;
+#pragma unroll
+        for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
+      }
+      if constexpr (PIPE) cp_async_wait<1>();  // V(t); K of the next tile may stay in flight
+      __syncwarp();
+      for (int j = 0; j < nk; ++j) {
+        const uint16_t* vr = vt + (size_t)j * D + lane * DL;
+        float vv[DL];
+        if constexpr (DL == 2) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
+          vv[0] = bf_lo(w);
+          vv[1] = bf_hi(w);
+        } else if constexpr (DL == 4) {
+          const uint2 w = *reinterpret_cast<const uint2*>(vr);
+          vv[0] = bf_lo(w.x);
+          vv[1] = bf_hi(w.x);
+          vv[2] = bf_lo(w.y);
+          vv[3] = bf_hi(w.y);
+        } else {
+          const uint4 w = *reinterpret_cast<const uint4*>(vr);
+          vv[0] = bf_lo(w.x);
+          vv[1] = bf_hi(w.x);
+          vv[2] = bf_lo(w.y);
+          vv[3] = bf_hi(w.y);
+          vv[4] = bf_lo(w.z);
+          vv[5] = bf_hi(w.z);
+          vv[6] = bf_lo(w.w);
+          vv[7] = bf_hi(w.w);
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float pj = pw[h * 32 + j];
+#pragma unroll
+          for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
+        }
+      }
+      __syncwarp();
+      if constexpr (PIPE) {
+        if (t + NW < t1) stage_v(t + NW);
+        else cp_async_commit();
+      }
+    }
+    if constexpr (PIPE) cp_async_wait<0>();
+
+    // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
+    attn_sync();
+    if (lane == 0)
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        wm[warp * G + h] = m[h];
+        wl[warp * G + h] = l[h];
+      }
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int e = 0; e < DL; ++e) wacc[((size_t)warp * G + h) * D + lane * DL + e] = acc[h][e];
+  }
   attn_sync();
 
   const int outw = geo.heads * D;

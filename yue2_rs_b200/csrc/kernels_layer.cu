@@ -450,9 +450,16 @@ __global__ void __launch_bounds__(128) attn_pipe_kernel(const AttnParams a) {
   attn_item<D, G, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
 }
 
-static int attention_smem_need(int dim, int groups, bool pipe = false) {
+// The pipelined loop with scores and P.V on the tensor cores (dim <= 128).
+template <int D, int G>
+__global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  attn_item<D, G, true, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+}
+
+static int attention_smem_need(int dim, int groups, bool pipe = false, bool mma = false) {
   const int tiles = (pipe ? 3 : 2) * 4 * 32 * dim * 2;
-  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4;
+  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4 + (mma ? 16 * dim * 2 : 0);
   const int merge = 4 * groups * dim * 4;
   return (tiles > merge ? tiles : merge) + extra;
 }
@@ -469,20 +476,34 @@ int attention_smem_bytes(int dim, int groups) {
 // than kMaxRows rows, which launch many waves of CTAs streaming many tiles per warp;
 // for the others when the caller asks (p.pipe: long contexts). YUE2_CUDA_ATTN_PIPE=1 / 0
 // forces it on / off everywhere.
+static int env_mode(const char* name) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : -1;
+}
 static int attn_pipe_mode() {
-  static int mode = [] {
-    const char* v = getenv("YUE2_CUDA_ATTN_PIPE");
-    return v && *v ? atoi(v) : -1;
-  }();
+  static int mode = env_mode("YUE2_CUDA_ATTN_PIPE");
+  return mode;
+}
+// Tensor-core scores and P.V (dim <= 128) wherever the pipelined loop runs;
+// YUE2_CUDA_ATTN_MMA=0 keeps the SIMT loop there, =1 uses the tensor cores everywhere.
+static int attn_mma_mode() {
+  static int mode = env_mode("YUE2_CUDA_ATTN_MMA");
   return mode;
 }
 
 template <int D, int G>
 static cudaError_t attn_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
-  const int mode = attn_pipe_mode();
+  const int mode = attn_pipe_mode(), mm = attn_mma_mode();
   const bool pipe = mode == 1 || (mode != 0 && (R > kMaxRows || p.pipe));
+  const bool mma = D <= 128 && (mm == 1 || (mm != 0 && pipe));
   const void* fn = pipe ? (const void*)attn_pipe_kernel<D, G> : (const void*)attn_kernel<D, G>;
-  const int smem = pipe ? attention_smem_need(D, G, true) : attention_smem_bytes(D, G);
+  int smem = pipe ? attention_smem_need(D, G, true) : attention_smem_bytes(D, G);
+  if constexpr (D <= 128) {
+    if (mma) {
+      fn = (const void*)attn_mma_kernel<D, G>;
+      smem = attention_smem_need(D, G, true, true);
+    }
+  }
   cudaError_t e = ensure_smem_attr(fn, smem);
   if (e != cudaSuccess || g_configure_only) return e;
   AttnParams copy = p;
