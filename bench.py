@@ -176,6 +176,11 @@ def main():
     ap.add_argument("--profile-songs", type=int, default=1, metavar="B",
                     help="with --profile: B songs (2B CFG rows) of 16-id prompts after a synthetic "
                          "1,008-position context")
+    ap.add_argument("--profile-context", type=int, default=0, metavar="L",
+                    help="with --profile: 16-id prompts after a synthetic (L - 16)-position context")
+    ap.add_argument("--profile-layers", type=int, default=0, metavar="N",
+                    help="with --profile: a model of N layers (same shapes otherwise), for ncu captures "
+                         "that must stay small")
     ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
                     help="one N-id prefill of the config-1 model and exit: the command line for the "
                          "prefill's ncu launch list")
@@ -200,6 +205,8 @@ def main():
         return dp.max(x)
 
     cfg = synth.config_c2()
+    if args.profile and args.profile_layers > 0:
+        cfg.num_hidden_layers = args.profile_layers
     model = Model.synthetic(cfg, seed=1, std=0.02, device=local)
     if args.prefill_profile:
         ids = np.random.default_rng(5).integers(0, cfg.vocab_size, args.prefill_profile).tolist()
@@ -211,16 +218,14 @@ def main():
         dp.close()
         return 0
     W, K = max(args.warmup, 3), args.steps
-    max_tokens = max(512, W + K + 1)
+    max_tokens = W + K + 1 if args.profile else max(512, W + K + 1)
     cond, uncond = prompts(1000 + rank, cfg.vocab_size)
     reqs = [Request(cond, seed=rank, negative=uncond, scale=SCALE)]
     if args.profile:
         B = max(1, args.profile_songs)
-        if B == 1:
-            reqs = [Request(cond[:16], seed=rank, negative=uncond[:16], scale=SCALE)]
-        else:
-            reqs = [Request(cond[16 * i: 16 * i + 16], seed=rank + i, negative=uncond[16 * i: 16 * i + 16], scale=SCALE,
-                            context_fill=PROMPT - 16) for i in range(B)]
+        fill = max(0, args.profile_context - 16) if args.profile_context else (PROMPT - 16 if B > 1 else 0)
+        reqs = [Request(cond[16 * i: 16 * i + 16], seed=rank + i, negative=uncond[16 * i: 16 * i + 16], scale=SCALE,
+                        context_fill=fill) for i in range(B)]
         args.no_sweep = args.no_cpu_baseline = True
     s = c2_sampling(max_tokens)
 

@@ -110,11 +110,12 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   // preceding kernel (prefill rows): it is never fetched before the wait
   const int first_tile = t0 + warp;
   const bool early = STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
-  // PIPE: K (swizzled) of tile t into buffer buf, V of tile t; one commit group each
-  auto stage_k = [&](int t, int buf) {
+  // PIPE: K (swizzled) of tile t into buffer buf, V of tile t; one commit group each. The
+  // page base comes from the caller (fetched a tile ahead, off the issue path).
+  auto page_of = [&](int t) { return reinterpret_cast<const uint16_t*>(row.pages[(t << 5) >> kPageLog2]); };
+  auto stage_k = [&](int t, int buf, const uint16_t* page) {
     const int key0 = t << 5;
     const int nk = min(32, keys - key0);
-    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
     const uint16_t* kb = page + koff + (size_t)(key0 & (kPageTokens - 1)) * D;
     uint16_t* dst = kt + (size_t)buf * 32 * D;
     for (int i = lane; i < 32 * CPR; i += 32) {
@@ -123,10 +124,9 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
     cp_async_commit();
   };
-  auto stage_v = [&](int t) {
+  auto stage_v = [&](int t, const uint16_t* page) {
     const int key0 = t << 5;
     const int nk = min(32, keys - key0);
-    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
     const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
     for (int i = lane; i < 32 * CPR; i += 32) {
       const int j = i / CPR, c = i % CPR;
@@ -140,8 +140,9 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   };
   if (early) {
     if constexpr (PIPE) {
-      stage_k(first_tile, 0);
-      stage_v(first_tile);
+      const uint16_t* p0 = page_of(first_tile);
+      stage_k(first_tile, 0, p0);
+      stage_v(first_tile, p0);
     } else {
       stage(first_tile);
     }
@@ -220,15 +221,18 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float mrow = -INFINITY, lrow = 0.f;  // head g8
     if (first_tile < t1 && !early) {
-      stage_k(first_tile, 0);
-      stage_v(first_tile);
+      const uint16_t* p0 = page_of(first_tile);
+      stage_k(first_tile, 0, p0);
+      stage_v(first_tile, p0);
     }
+    const uint16_t* pnext = first_tile + NW < t1 ? page_of(first_tile + NW) : nullptr;
     for (int t = first_tile, it = 0; t < t1; t += NW, ++it) {
       const int nk = min(32, keys - (t << 5));
       const unsigned char* kb = reinterpret_cast<const unsigned char*>(kt + (size_t)(it & 1) * 32 * D);
       const unsigned char* vb = reinterpret_cast<const unsigned char*>(vt);
-      if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
+      if (t + NW < t1) stage_k(t + NW, (it + 1) & 1, pnext);
       else cp_async_commit();
+      const uint16_t* pafter = t + 2 * NW < t1 ? page_of(t + 2 * NW) : nullptr;  // in flight meanwhile
       cp_async_wait<2>();
       __syncwarp();
       float s[4][4];
@@ -294,8 +298,9 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
         }
       }
       __syncwarp();
-      if (t + NW < t1) stage_v(t + NW);
+      if (t + NW < t1) stage_v(t + NW, pnext);
       else cp_async_commit();
+      pnext = pafter;
     }
     cp_async_wait<0>();
     // ---- merge the warps of this CTA (tiles reused as [NW][G][D] f32 accumulators)
@@ -322,17 +327,24 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
     float* pw = ps + warp * G * 32;
 
-    if (PIPE && first_tile < t1 && !early) {
-      stage_k(first_tile, 0);
-      stage_v(first_tile);
+    const uint16_t* pnext = nullptr;
+    if constexpr (PIPE) {
+      if (first_tile < t1 && !early) {
+        const uint16_t* p0 = page_of(first_tile);
+        stage_k(first_tile, 0, p0);
+        stage_v(first_tile, p0);
+      }
+      pnext = first_tile + NW < t1 ? page_of(first_tile + NW) : nullptr;
     }
     for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
       const int key0 = t << 5;
       const int nk = min(32, keys - key0);
       const uint16_t* kcur = kt + (PIPE ? (size_t)(it & 1) * 32 * D : 0);
+      const uint16_t* pafter = nullptr;
       if constexpr (PIPE) {
-        if (t + NW < t1) stage_k(t + NW, (it + 1) & 1);
+        if (t + NW < t1) stage_k(t + NW, (it + 1) & 1, pnext);
         else cp_async_commit();  // keeps the group count: K(t) is third from the end
+        pafter = t + 2 * NW < t1 ? page_of(t + 2 * NW) : nullptr;
         cp_async_wait<2>();
       } else {
         if (!(early && t == first_tile)) stage(t);
@@ -413,8 +425,9 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
       }
       __syncwarp();
       if constexpr (PIPE) {
-        if (t + NW < t1) stage_v(t + NW);
+        if (t + NW < t1) stage_v(t + NW, pnext);
         else cp_async_commit();
+        pnext = pafter;
       }
     }
     if constexpr (PIPE) cp_async_wait<0>();
