@@ -154,6 +154,17 @@ int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void*
 int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float std, float norm_mean);
 /* Checks that every AR tensor is present and prepares RoPE tables and workspaces. */
 int yue2_model_finalize(Yue2Model* m);
+/* Model::open's tensor reads (src/model.rs:418-451) over Weights::open
+ * (src/checkpoint.rs:315-396): the checkpoint directory `dir` holds model.safetensors or
+ * model.safetensors.index.json + shards. Headers are validated as the reference does
+ * (header size, dtype F32/BF16/F16, extents, duplicates, overlaps, shard paths); every
+ * tensor on the AR decode path is uploaded (BF16 matrices through pinned double-buffered
+ * staging; gains and F32/F16 matrices converted as yue2_model_set_tensor does). Other
+ * tensors (NAR, latent, VAE bridges) are skipped. `bytes_uploaded` (nullable) receives the
+ * bytes copied to the device. Call yue2_model_finalize afterwards. */
+int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_uploaded);
+/* Header validation only (no device needed): the number of tensors in the checkpoint. */
+int yue2_checkpoint_scan(const char* dir, uint64_t* tensors);
 /* Copies a device tensor back as bf16 bits (count elements). */
 int yue2_model_get_tensor(Yue2Model* m, const char* name, uint16_t* out, uint64_t count);
 void yue2_model_free(Yue2Model* m);

@@ -89,6 +89,8 @@ _PROTOS = {
     "yue2_model_set_tensor": (c_int, [c_p, ctypes.c_char_p, c_int, c_p, c_u64, c_u64]),
     "yue2_model_init_synthetic": (c_int, [c_p, c_u64, c_f, c_f]),
     "yue2_model_finalize": (c_int, [c_p]),
+    "yue2_model_load_checkpoint": (c_int, [c_p, ctypes.c_char_p, ctypes.POINTER(c_u64)]),
+    "yue2_checkpoint_scan": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_u64)]),
     "yue2_model_get_tensor": (c_int, [c_p, ctypes.c_char_p, c_p, c_u64]),
     "yue2_model_free": (None, [c_p]),
     "yue2_cache_create": (c_int, [c_p, c_u64, ctypes.POINTER(c_p)]),

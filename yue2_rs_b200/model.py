@@ -98,12 +98,17 @@ class Model:
 
     # ---- construction
     @classmethod
-    def open(cls, path, device=0):
-        """Model::open (src/model.rs:418-451): config.json + safetensors under `path`."""
+    def open(cls, path, device=0, loader="native"):
+        """Model::open (src/model.rs:418-451): config.json + safetensors under `path`. The
+        native loader (yue2_model_load_checkpoint) validates the headers and uploads through
+        pinned staging; loader="python" reads with numpy and calls set_tensor per tensor."""
         m = cls(Config.read(os.path.join(path, "config.json")), device)
-        for name, code, shape, arr in checkpoint.tensors(path):
-            rows, cols = (shape[0], int(np.prod(shape[1:]))) if len(shape) > 1 else (1, shape[0] if shape else 1)
-            m.set_tensor(name, arr, code, rows, cols)
+        if loader == "native":
+            _lib.check(_lib.lib().yue2_model_load_checkpoint(m._h, os.fsencode(path), None))
+        else:
+            for name, code, shape, arr in checkpoint.tensors(path):
+                rows, cols = (shape[0], int(np.prod(shape[1:]))) if len(shape) > 1 else (1, shape[0] if shape else 1)
+                m.set_tensor(name, arr, code, rows, cols)
         m.finalize()
         return m
 
