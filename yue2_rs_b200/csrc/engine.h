@@ -142,6 +142,7 @@ int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n,
 int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase);
 int ensure_wide(Yue2Model& m);
 int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase);
+int prepare_wide(Yue2Model& m, int R, int phase);
 int wide_kernels_per_step(const Yue2Model& m, int phase);
 constexpr int kMaxWideRows = 256;    // rows of a wide decode step (128 songs with CFG)
 constexpr int kPrefillGemmMin = 64;  // shorter prompts go through the GEMV chain in 16-row chunks

@@ -234,20 +234,50 @@ static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16
     cublasLtMatmulPreference_t pref = nullptr;
     const uint32_t no_split = m.gemm_split_k ? (uint32_t)CUBLASLT_REDUCTION_SCHEME_COMPUTE_TYPE
                                              : (uint32_t)CUBLASLT_REDUCTION_SCHEME_NONE;
-    cublasLtMatmulHeuristicResult_t res{};
+    constexpr int kCand = 8;
+    cublasLtMatmulHeuristicResult_t res[kCand] = {};
     int found = 0;
     if ((st = cublasLtMatmulPreferenceCreate(&pref)) ||
         (st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &P.ws_bytes,
                                                    sizeof(P.ws_bytes))) ||
         (st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_REDUCTION_SCHEME_MASK, &no_split,
                                                    sizeof(no_split))) ||
-        (st = cublasLtMatmulAlgoGetHeuristic(P.lt, gm.op, gm.a, gm.b, gm.d, gm.d, pref, 1, &res, &found))) {
+        (st = cublasLtMatmulAlgoGetHeuristic(P.lt, gm.op, gm.a, gm.b, gm.d, gm.d, pref, kCand, res, &found))) {
       if (pref) cublasLtMatmulPreferenceDestroy(pref);
       return lt_fail(st, "cuBLASLt heuristic");
     }
     cublasLtMatmulPreferenceDestroy(pref);
     if (found < 1) return fail(YUE2_ERR_CUDA, "cuBLASLt has no algorithm for a prefill GEMM");
-    gm.algo = res.algo;
+    // Time the candidates once on the call's own operands (outside a stream capture; the
+    // output is rewritten by the call itself) and keep the fastest; inside a capture the
+    // heuristic's first choice stands.
+    gm.algo = res[0].algo;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (found > 1 && cudaStreamIsCapturing(m.stream, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      float best = 1e30f;
+      if (cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess) {
+        const float alpha = 1.f, beta = 0.f;
+        for (int i = 0; i < found; ++i) {
+          bool ok = cublasLtMatmul(P.lt, gm.op, &alpha, W, gm.a, X, gm.b, &beta, Y, gm.d, Y, gm.d, &res[i].algo, P.ws,
+                                   P.ws_bytes, m.stream) == CUBLAS_STATUS_SUCCESS;
+          cudaEventRecord(e0, m.stream);
+          for (int rep = 0; ok && rep < 3; ++rep)
+            ok = cublasLtMatmul(P.lt, gm.op, &alpha, W, gm.a, X, gm.b, &beta, Y, gm.d, Y, gm.d, &res[i].algo, P.ws,
+                                P.ws_bytes, m.stream) == CUBLAS_STATUS_SUCCESS;
+          cudaEventRecord(e1, m.stream);
+          float ms = 0.f;
+          if (ok && cudaEventSynchronize(e1) == cudaSuccess && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess &&
+              ms < best) {
+            best = ms;
+            gm.algo = res[i].algo;
+          }
+        }
+      }
+      if (e0) cudaEventDestroy(e0);
+      if (e1) cudaEventDestroy(e1);
+      CK(cudaGetLastError());
+    }
     it = P.gemms.emplace(key, gm).first;
   }
   const LtGemm& gm = it->second;
@@ -449,6 +479,33 @@ int ensure_wide(Yue2Model& m) {
   m.wide_rows = (DevRow*)a;
   m.wide_logits = (float*)b;
   m.wide_head = (uint16_t*)c;
+  return 0;
+}
+
+// Runs each GEMM shape of a wide step once, outside any stream capture, so that its
+// algorithm is timed and chosen before a session graph captures the step. The operands are
+// workspace buffers (their contents do not matter; the outputs are scratch).
+int prepare_wide(Yue2Model& m, int R, int phase) {
+  int rc = ensure_wide(m);
+  if (rc) return rc;
+  PrefillBufs& P = *m.prefill;
+  const Geometry& g = m.g;
+  const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
+  const LayerW& w = m.layers[0];
+  const uint16_t* Wqkv[3] = {w.q, w.k, w.v};
+  const int Nqkv[3] = {qd, kd, kd};
+  const uint16_t* Wgu[2] = {w.gate, w.up};
+  const int Ngu[2] = {I, I};
+  int lo, hi, start, end, stop;
+  head_span(m, phase, lo, hi, start, end, stop);
+  const int n = hi - lo, ldh = (n + 7) & ~7;
+  if ((rc = gemm_concat(m, Wqkv, Nqkv, 3, H, P.xb, H, P.qkv, qd + 2 * kd, R)) ||
+      (rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, R)) ||
+      (rc = gemm_concat(m, Wgu, Ngu, 2, H, P.xb, H, P.gu, 2 * I, R)) ||
+      (rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, R)) ||
+      (rc = gemm_bf16(m, m.lm_head + (size_t)lo * H, n, H, P.xb, H, m.wide_head, ldh, R)))
+    return rc;
+  CK(cudaStreamSynchronize(m.stream));
   return 0;
 }
 
