@@ -326,7 +326,7 @@ def main():
         batched[str(B)] = {"songs_per_gpu": B, "rows": 2 * B, "tokens_per_s": world * B * ks / (bms / 1000.0),
                            "ms_per_step": bms / ks, "context_mid": ctx, "step_bytes": sb,
                            "hbm_frac_of_measured": sb / (bms / ks * 1e-3) / 1e9 / peak,
-                           "forward": "gemv" if 2 * B <= 16 else "gemm"}
+                           "forward": "gemm"}
 
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()

@@ -280,6 +280,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     const char* a = getenv("YUE2_CUDA_PREFILL_ATTN");
     m->prefill_tc_attn = !(a && std::string(a) == "rows");
     m->gemm_split_k = env_int("YUE2_CUDA_GEMM_SPLITK", 0) != 0;
+    m->wide_min = std::max(2, std::min(kMaxRows + 1, env_int("YUE2_CUDA_WIDE_MIN", 3)));
   }
   *out = m;
   return 0;
@@ -947,7 +948,7 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
     dr[r].advance = 1;
   }
   const float* out = m->logits;
-  if (rows > (uint64_t)kMaxRows) {  // the GEMM path (gemm_rows.cu)
+  if (rows >= (uint64_t)m->wide_min) {  // the GEMM path (gemm_rows.cu)
     if ((rc = ensure_wide(*m))) return rc;
     CK(cudaMemcpyAsync(m->wide_rows, dr.data(), rows * sizeof(DevRow), cudaMemcpyHostToDevice, m->stream));
     if ((rc = encode_forward_wide(*m, m->stream, (int)rows, phase))) return rc;

@@ -56,6 +56,7 @@ struct Yue2Model {
   int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
   bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
+  int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
   y2::PrefillBufs* prefill = nullptr;
   // decode steps of more than kMaxRows rows (the GEMM path): row descriptors, logits
   // [kMaxWideRows, vocab] and the bf16 LM head output
@@ -145,6 +146,6 @@ int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase);
 int prepare_wide(Yue2Model& m, int R, int phase);
 int wide_kernels_per_step(const Yue2Model& m, int phase);
 constexpr int kMaxWideRows = 256;    // rows of a wide decode step (128 songs with CFG)
-constexpr int kPrefillGemmMin = 64;  // shorter prompts go through the GEMV chain in 16-row chunks
+constexpr int kPrefillGemmMin = 3;   // shorter prompts go through the GEMV chain
 constexpr int kPrefillRows = 1024;   // capacity of the GEMM prefill buffers, in rows
 }  // namespace y2

@@ -289,7 +289,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
   if (R > kMaxWideRows)
     return fail(YUE2_ERR_INVALID, "at most 256 decode rows (CFG rows count twice) per session");
   if ((rc = y2_set_device(m))) return rc;
-  const bool wide = R > kMaxRows;  // the GEMM path (gemm_rows.cu) past 16 rows
+  const bool wide = R >= m->wide_min;  // the GEMM path (gemm_rows.cu), past 16 rows by default
   if (wide && (rc = ensure_wide(*m))) return rc;
   Yue2Session* ss = new Yue2Session();
   ss->m = m;

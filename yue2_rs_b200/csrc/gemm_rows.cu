@@ -338,6 +338,7 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, DevRow* rows, int l, int 
   ap.sin_tab = m.sin_tab;
   ap.max_pos = m.max_pos;
   ap.error = m.flags + 1;
+  ap.pipe = fused ? 1 : 0;  // decode rows of the GEMM path: the pipelined tensor-core loop
   CK(launch_attention(m.stream, false, ap, R));
   return 0;
 }
