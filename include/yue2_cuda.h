@@ -182,7 +182,7 @@ int yue2_cache_read(const Yue2Cache* c, uint64_t layer, uint64_t begin, uint64_t
                     uint16_t* v);
 
 /* Model::forward / forward_phase (src/model.rs:465-477) for `rows` (<= 256) distinct caches
- * at once, one new id per cache; logits [rows, vocab] (nullable). Up to 16 rows run as one
+ * at once, one new id per cache; logits [rows, vocab] (nullable). One or two rows run as a
  * weight-streaming GEMV pass, more as tensor-core GEMMs. YUE2_PHASE_VOCAB returns
  * the full LM-head row; ABC/SEMANTIC return project_phase's window + stop row with -inf
  * elsewhere (model.rs:478-507). */
@@ -234,8 +234,8 @@ typedef struct {
 /* sampling::generate (src/sampling.rs:222-294) for `n` independent songs sharing one
  * Sampling and phase (at most 256 rows per step: 128 songs with CFG; CFG rows count
  * twice): prefill (cond and, when scale != 1, uncond), then one graph launch per token:
- * both CFG rows of every song in one weight pass (GEMV up to 16 rows, tensor-core GEMMs
- * beyond), on-device CFG mix + choose. */
+ * both CFG rows of every song in one weight pass (GEMV for 1-2 rows, tensor-core GEMMs
+ * from 3 rows), on-device CFG mix + choose. */
 int yue2_generate(Yue2Model* m, const Yue2Sampling* s, int phase, Yue2Request* reqs, uint64_t n,
                   Yue2Timing* timing);
 

@@ -156,8 +156,8 @@ class Model:
         return Cache(self, capacity)
 
     def forward_rows(self, caches, ids, phase=Phase.VOCAB):
-        """One new id for each of up to 256 distinct caches in one pass (GEMV up to 16 rows, GEMMs
-        beyond); logits [rows, vocab]."""
+        """One new id for each of up to 256 distinct caches in one pass (GEMV for 1-2 rows, GEMMs
+        from 3); logits [rows, vocab]."""
         n = len(caches)
         arr = (ctypes.c_void_p * n)(*[c._h for c in caches])
         ids = np.ascontiguousarray(ids, dtype=np.int64)
