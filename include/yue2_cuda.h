@@ -163,6 +163,13 @@ int yue2_model_finalize(Yue2Model* m);
  * tensors (NAR, latent, VAE bridges) are skipped. `bytes_uploaded` (nullable) receives the
  * bytes copied to the device. Call yue2_model_finalize afterwards. */
 int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_uploaded);
+/* Timing and parity hook for the prefill GEMMs: Y[C, N] = X[C, K] . W[N, K]^T on device
+ * bf16 buffers (row-major, dense), `reps` timed runs after one untimed; impl 0 = cuBLASLt,
+ * 1 = the tcgen05 kernel (K a multiple of 64), 2 = its gate|up form: W = [gate; up] of
+ * [2N, K] and Y = bf16(bf16(silu(bf16 g)) * bf16 u) of [C, N] (N a multiple of 128).
+ * `avg_ms` (nullable) gets the mean. */
+int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl, int reps,
+                    double* avg_ms);
 /* Header validation only (no device needed): the number of tensors in the checkpoint. */
 int yue2_checkpoint_scan(const char* dir, uint64_t* tensors);
 /* Copies a device tensor back as bf16 bits (count elements). */

@@ -91,6 +91,7 @@ _PROTOS = {
     "yue2_model_finalize": (c_int, [c_p]),
     "yue2_model_load_checkpoint": (c_int, [c_p, ctypes.c_char_p, ctypes.POINTER(c_u64)]),
     "yue2_checkpoint_scan": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_u64)]),
+    "yue2_bench_gemm": (c_int, [c_p, c_p, c_p, c_p, c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
     "yue2_model_get_tensor": (c_int, [c_p, ctypes.c_char_p, c_p, c_u64]),
     "yue2_model_free": (None, [c_p]),
     "yue2_cache_create": (c_int, [c_p, c_u64, ctypes.POINTER(c_p)]),

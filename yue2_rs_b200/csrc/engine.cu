@@ -281,6 +281,8 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     m->prefill_tc_attn = !(a && std::string(a) == "rows");
     m->gemm_split_k = env_int("YUE2_CUDA_GEMM_SPLITK", 0) != 0;
     m->wide_min = std::max(2, std::min(kMaxRows + 1, env_int("YUE2_CUDA_WIDE_MIN", 3)));
+    const char* gm = getenv("YUE2_CUDA_GEMM");
+    m->gemm_tc = gm && std::string(gm) == "tc";
   }
   *out = m;
   return 0;

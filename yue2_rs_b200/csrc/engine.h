@@ -57,6 +57,7 @@ struct Yue2Model {
   bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
+  bool gemm_tc = false;          // GEMMs of >= 128 rows on the tcgen05 kernel (YUE2_CUDA_GEMM=tc), else cuBLASLt
   y2::PrefillBufs* prefill = nullptr;
   // decode steps of more than kMaxRows rows (the GEMM path): row descriptors, logits
   // [kMaxWideRows, vocab] and the bf16 LM head output

@@ -215,8 +215,20 @@ static int ensure_prefill(Yue2Model& m) {
 // separate pass (YUE2_CUDA_GEMM_SPLITK=1; default: no split), never with in-place or
 // output-type partial sums, so a row's result depends only on the shapes and repeats
 // bit for bit.
+static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
+                   int C);
+
 static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
                      int C) {
+  if (m.gemm_tc && C >= 128 && gemm_tc_supported(C, N, K, ldx, ldy, X, W, Y)) {
+    CK(launch_gemm_tc(m.stream, W, N, K, X, ldx, Y, ldy, C, m.flags + 2));
+    return 0;
+  }
+  return gemm_lt(m, W, N, K, X, ldx, Y, ldy, C);
+}
+
+static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
+                   int C) {
   PrefillBufs& P = *m.prefill;
   const std::array<int, 5> key = {N, K, ldx, ldy, C};
   auto it = P.gemms.find(key);
@@ -398,12 +410,16 @@ static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const u
     }
     if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, R))) return rc;
     CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, R));
-    {
-      const uint16_t* W[2] = {w.gate, w.up};
-      const int N[2] = {I, I};
-      if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, R))) return rc;
-    }
-    {
+    if (m.gemm_tc && R >= 128 && w.up == w.gate + (size_t)I * H && I % 128 == 0 &&
+        gemm_tc_supported(R, I, H, H, I, P.xb, w.gate, P.h)) {
+      // gate|up GEMM with the SwiGLU epilogue fused (tcgen05)
+      CK(launch_gemm_tc_swiglu(s, w.gate, I, H, P.xb, H, P.h, I, R, m.flags + 2));
+    } else {
+      {
+        const uint16_t* W[2] = {w.gate, w.up};
+        const int N[2] = {I, I};
+        if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, R))) return rc;
+      }
       const uint16_t* gu = P.gu;
       uint16_t* h = P.h;
       int inter = I, nrows = R;
@@ -567,3 +583,41 @@ int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, i
 }
 
 }  // namespace y2
+
+// ---------------------------------------------------------------- GEMM timing and parity hook
+extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl,
+                               int reps, double* avg_ms) {
+  using namespace y2;
+  if (!m || !X || !W || !Y || C < 1 || N < 1 || K < 1 || reps < 1 || impl < 0 || impl > 2)
+    return fail(YUE2_ERR_INVALID, "bad GEMM benchmark arguments");
+  int rc = y2_set_device(m);
+  if (rc || (rc = ensure_prefill(*m))) return rc;
+  const uint16_t *x = (const uint16_t*)X, *w = (const uint16_t*)W;
+  uint16_t* y = (uint16_t*)Y;
+  if (impl >= 1 && (!gemm_tc_supported(C, N, K, K, N, X, W, Y) || (impl == 2 && N % 128)))
+    return fail(YUE2_ERR_INVALID, "shape not supported by the tcgen05 GEMM");
+  cudaEvent_t a = nullptr, b = nullptr;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  for (int i = 0; i <= reps && !rc; ++i) {
+    if (i == 1) cudaEventRecord(a, m->stream);
+    if (impl == 1) {
+      const cudaError_t e = launch_gemm_tc(m->stream, w, N, K, x, K, y, N, C, m->flags + 2);
+      if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_tc");
+    } else if (impl == 2) {
+      const cudaError_t e = launch_gemm_tc_swiglu(m->stream, w, N, K, x, K, y, N, C, m->flags + 2);
+      if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_tc_swiglu");
+    } else {
+      rc = gemm_lt(*m, w, N, K, x, K, y, N, C);
+    }
+  }
+  cudaEventRecord(b, m->stream);
+  cudaEventSynchronize(b);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (rc) return rc;
+  if (avg_ms) *avg_ms = ms / reps;
+  return take_flags(*m);
+}

@@ -198,6 +198,11 @@ cudaError_t launch_with(cudaStream_t s, bool pdl, dim3 grid, dim3 block, size_t 
 cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R);
 cudaError_t launch_attention(cudaStream_t s, bool pdl, const AttnParams& p, int R);
 bool prefill_attention_supported(const Geometry& g);
+bool gemm_tc_supported(int C, int N, int K, int ldx, int ldy, const void* X, const void* W, const void* Y);
+cudaError_t launch_gemm_tc(cudaStream_t s, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y,
+                           int ldy, int C, int32_t* error);
+cudaError_t launch_gemm_tc_swiglu(cudaStream_t s, const uint16_t* Wgu, int I, int K, const uint16_t* X, int ldx,
+                                  uint16_t* H, int ldh, int C, int32_t* error);
 cudaError_t launch_prefill_attention(cudaStream_t s, const PrefillAttnParams& p);
 cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R);
 cudaError_t launch_mt_words(cudaStream_t s, MtState* st, uint32_t* words, int nwords, const SampleReq* reqs,

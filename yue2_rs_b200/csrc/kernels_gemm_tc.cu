@@ -1,0 +1,314 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) for the
+// prefill chunks: Y[C, N] = X[C, K] . W[N, K]^T, f32 accumulation, bf16 output rounded to
+// nearest even (Linear::finish's rounding, src/tensor.rs:1102-1118).
+//
+// One CTA computes a 128 x 256 output tile (128 rows of X, 256 rows of W): 6 warps.
+//   warp 0       TMA producer: 64-column K blocks of X and W (128B-swizzled) into a
+//                4-stage shared-memory ring, completion counted on the stage's mbarrier
+//   warp 1       allocates 256 TMEM columns; one lane issues tcgen05.mma (M 128, N 256,
+//                K 16; four per K block), and tcgen05.commit frees each stage and finally
+//                signals the accumulator
+//   warps 2-5    epilogue: tcgen05.ld of their TMEM lane quarter, bf16 rounding, stores
+// The SwiGLU form (gate|up of Mlp::apply, src/model.rs:206-214) takes the 256 B rows of a
+// tile as 128 gate rows and the 128 up rows of the same outputs (W = [gate; up], up at row
+// `inter`), and its epilogue writes h = bf16(bf16(silu(bf16 g)) * bf16 u) for 128 outputs,
+// exactly the rounding of the unfused GEMM + swiglu kernel pair.
+// Every mbarrier wait is bounded: after kSpin polls it sets *error and the CTA still
+// reaches the final barrier, where warp 1 frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace y2 {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr long kSpin = 1L << 22;
+
+struct TcGemmArgs {
+  uint16_t* Y;
+  int ldy, C, N, K;
+  int inter;  // SwiGLU form: row of W where the up rows start; N = outputs (= inter)
+  int32_t* error;
+};
+
+Y2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+Y2_DEV void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+Y2_DEV void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+Y2_DEV bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity; false (and *error set) when it gave up.
+Y2_DEV bool mbar_wait(uint64_t* b, uint32_t parity, int32_t* error) {
+  for (long i = 0; i < kSpin; ++i)
+    if (mbar_try_wait(b, parity)) return true;
+  atomicExch(error, 1);
+  return false;
+}
+
+Y2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of
+// 128 B, 8-row groups 1024 B apart (stride byte offset), descriptor version 1.
+Y2_DEV uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;              // leading byte offset (unused by swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
+  d |= (uint64_t)1 << 46;              // version
+  d |= (uint64_t)2 << 61;              // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: dense, D f32, A and B bf16, both K-major, N = BN, M = BM.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+Y2_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+Y2_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+Y2_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+Y2_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+Y2_DEV void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 bf16 outputs (packed in pairs) of one row: four 16-byte stores, or element stores at
+// the ragged right edge of the matrix.
+Y2_DEV void store32(uint16_t* dst, const uint32_t (&w)[16], int valid) {
+  if (valid >= 32) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  } else {
+    for (int i = 0; i < valid; ++i) dst[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+  }
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                   const TcGemmArgs p) {
+  constexpr int NOUT = SWIGLU ? BN / 2 : BN;  // output columns per tile
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte aligned ring (the swizzle pattern and the descriptors assume it)
+  unsigned char* ring = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * NOUT, m0 = blockIdx.y * BM;
+  const int nk = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !mbar_wait(empty + s, ((kb / STAGES) - 1) & 1, p.error)) break;
+        unsigned char* a = ring + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(full + s, STAGE_BYTES);
+        tma_load_2d(a, &tmx, full + s, kb * BK, m0);
+        if (SWIGLU) {  // gate rows n0.., then up rows inter + n0..
+          tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
+          tma_load_2d(a + A_BYTES + B_BYTES / 2, &tmw, full + s, kb * BK, p.inter + n0);
+        } else {
+          tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(full + s, (kb / STAGES) & 1, p.error)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(ring + s * STAGE_BYTES), b = a + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)  // 16 columns = 32 bytes along the swizzled row
+          umma_bf16(tmem, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) != 0);
+        umma_commit(empty + s);  // frees the stage once these MMAs have read it
+      }
+      umma_commit(accum);  // all issued MMAs complete (also on the error path)
+    }
+  } else {  // epilogue: warps 2-5 read TMEM lanes 32 * (warp % 4) .. + 31
+    const int q = warp & 3;
+    if (mbar_wait(accum, 0, p.error)) {
+      tc_fence_after();
+      const int row = m0 + 32 * q + lane;
+      const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+      for (int c0 = 0; c0 < NOUT; c0 += 32) {
+        uint32_t w[16];
+        if constexpr (SWIGLU) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tl + (uint32_t)c0, g);
+          tmem_ld32(tl + (uint32_t)(NOUT + c0), u);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float h2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float gv = round_bf16(__uint_as_float(g[2 * i + e]));
+              const float uv = round_bf16(__uint_as_float(u[2 * i + e]));
+              const float act = round_bf16(gv / (1.0f + det_expf(-gv)));
+              h2[e] = act * uv;
+            }
+            w[i] = pack_bf16x2(h2[0], h2[1]);
+          }
+        } else {
+          uint32_t v[32];
+          tmem_ld32(tl + (uint32_t)c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        }
+        if (row < p.C && n0 + c0 < p.N) store32(p.Y + (size_t)row * p.ldy + n0 + c0, w, p.N - n0 - c0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  }
+}
+
+// The driver's tensor-map encoder, looked up through the runtime (the library does not link
+// the driver, so that it loads on machines without one).
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2D tensor map of a row-major bf16 matrix [rows, cols] with row stride ld elements, boxes of
+// 64 columns (128 bytes, 128-byte swizzle) x box_rows rows; out-of-range rows read as zero.
+bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, int box_rows) {
+  const auto encode = encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kTcGemmSmem = STAGES * STAGE_BYTES + 1024 + 256;
+
+template <bool SWIGLU>
+cudaError_t set_smem_once() {
+  static int set_dev = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || set_dev == dev) return e;
+  e = cudaFuncSetAttribute((const void*)gemm_tc_kernel<SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kTcGemmSmem);
+  if (e == cudaSuccess) set_dev = dev;
+  return e;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int C, int N, int K, int ldx, int ldy, const void* X, const void* W, const void* Y) {
+  return C >= 1 && N >= 1 && K >= BK && K % BK == 0 && ldx % 8 == 0 && ldy % 8 == 0 && ldx >= K && ldy >= N &&
+         ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)Y & 15) == 0;
+}
+
+cudaError_t launch_gemm_tc(cudaStream_t s, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y,
+                           int ldy, int C, int32_t* error) {
+  if (!gemm_tc_supported(C, N, K, ldx, ldy, X, W, Y)) return cudaErrorInvalidValue;
+  cudaError_t e = set_smem_once<false>();
+  if (e != cudaSuccess) return e;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, X, C, K, ldx, BM) || !make_map(&mw, W, N, K, K, BN)) return cudaErrorInvalidValue;
+  TcGemmArgs a{Y, ldy, C, N, K, 0, error};
+  void* args[] = {&mx, &mw, &a};
+  const dim3 grid((N + BN - 1) / BN, (C + BM - 1) / BM);
+  return launch_with(s, false, grid, dim3(THREADS), kTcGemmSmem, (const void*)gemm_tc_kernel<false>, args);
+}
+
+// h[C, I] = bf16(bf16(silu(bf16(X . Wg^T))) * bf16(X . Wu^T)) with Wgu = [Wg; Wu] ([2I, K]).
+cudaError_t launch_gemm_tc_swiglu(cudaStream_t s, const uint16_t* Wgu, int I, int K, const uint16_t* X, int ldx,
+                                  uint16_t* H, int ldh, int C, int32_t* error) {
+  if (I % (BN / 2) || !gemm_tc_supported(C, I, K, ldx, ldh, X, Wgu, H)) return cudaErrorInvalidValue;
+  cudaError_t e = set_smem_once<true>();
+  if (e != cudaSuccess) return e;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, X, C, K, ldx, BM) || !make_map(&mw, Wgu, 2 * I, K, K, BN / 2)) return cudaErrorInvalidValue;
+  TcGemmArgs a{H, ldh, C, I, K, I, error};
+  void* args[] = {&mx, &mw, &a};
+  const dim3 grid(I / (BN / 2), (C + BM - 1) / BM);
+  return launch_with(s, false, grid, dim3(THREADS), kTcGemmSmem, (const void*)gemm_tc_kernel<true>, args);
+}
+
+}  // namespace y2
