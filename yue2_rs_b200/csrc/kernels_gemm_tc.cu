@@ -2,13 +2,17 @@
 // prefill chunks: Y[C, N] = X[C, K] . W[N, K]^T, f32 accumulation, bf16 output rounded to
 // nearest even (Linear::finish's rounding, src/tensor.rs:1102-1118).
 //
-// One CTA computes a 128 x 256 output tile (128 rows of X, 256 rows of W): 6 warps.
+// A persistent grid (one CTA per SM) walks 128 x 256 output tiles (128 rows of X, 256 rows
+// of W), with two TMEM accumulators so that the epilogue of one tile overlaps the MMAs of
+// the next: 10 warps.
 //   warp 0       TMA producer: 64-column K blocks of X and W (128B-swizzled) into a
 //                4-stage shared-memory ring, completion counted on the stage's mbarrier
-//   warp 1       allocates 256 TMEM columns; one lane issues tcgen05.mma (M 128, N 256,
-//                K 16; four per K block), and tcgen05.commit frees each stage and finally
-//                signals the accumulator
-//   warps 2-5    epilogue: tcgen05.ld of their TMEM lane quarter, bf16 rounding, stores
+//   warp 1       allocates all 512 TMEM columns (two accumulators); one lane issues
+//                tcgen05.mma (M 128, N 256, K 16; four per K block), and tcgen05.commit
+//                frees each stage and signals each finished accumulator
+//   warps 2-9    epilogue, two warps per TMEM lane quarter (each half of the columns):
+//                tcgen05.ld, bf16 rounding, stores; then each warp arrives on the
+//                accumulator's "drained" barrier
 // The SwiGLU form (gate|up of Mlp::apply, src/model.rs:206-214) takes the 256 B rows of a
 // tile as 128 gate rows and the 128 up rows of the same outputs (W = [gate; up], up at row
 // `inter`), and its epilogue writes h = bf16(bf16(silu(bf16 g)) * bf16 u) for 128 outputs,
@@ -16,6 +20,8 @@
 // Every mbarrier wait is bounded: after kSpin polls it sets *error and the CTA still
 // reaches the final barrier, where warp 1 frees its TMEM.
 #include <cuda.h>
+#include <algorithm>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
@@ -25,9 +31,13 @@
 namespace y2 {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
+constexpr int BM = 128, BK = 64, STAGES = 4, TMEM_COLS = 512;
+constexpr int A_BYTES = BM * BK * 2;
+// per tile width BN (rows of W): bytes of a W block and of a stage
+template <int BN> __host__ __device__ constexpr int b_bytes() { return BN * BK * 2; }
+template <int BN> __host__ __device__ constexpr int stage_bytes() { return A_BYTES + b_bytes<BN>(); }
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each taking half of the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr long kSpin = 1L << 22;
 
 struct TcGemmArgs {
@@ -84,15 +94,18 @@ Y2_DEV uint64_t sdesc_sw128(uint32_t saddr) {
 }
 
 // Instruction descriptor: dense, D f32, A and B bf16, both K-major, N = BN, M = BM.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
+template <int BN>
 Y2_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc<BN>()), "r"(accumulate)
       : "memory");
 }
 Y2_DEV void umma_commit(uint64_t* bar) {
@@ -127,21 +140,24 @@ Y2_DEV void store32(uint16_t* dst, const uint32_t (&w)[16], int valid) {
   }
 }
 
-template <bool SWIGLU>
+template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                    const TcGemmArgs p) {
   constexpr int NOUT = SWIGLU ? BN / 2 : BN;  // output columns per tile
+  constexpr int B_BYTES = b_bytes<BN>(), STAGE_BYTES = stage_bytes<BN>();
+  static_assert(BN % 32 == 0 && (NOUT / 2) % 32 == 0 && 2 * BN <= TMEM_COLS, "tile width");
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte aligned ring (the swizzle pattern and the descriptors assume it)
   unsigned char* ring = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* afull = empty + STAGES;  // [2] accumulator b complete (MMA -> epilogue)
+  uint64_t* aempty = afull + 2;      // [2] accumulator b drained (epilogue warps -> MMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * NOUT, m0 = blockIdx.y * BM;
+  const int mt = (p.C + BM - 1) / BM, tiles = mt * ((p.N + NOUT - 1) / NOUT);
   const int nk = p.K / BK;
 
   if (threadIdx.x == 0) {
@@ -149,12 +165,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(afull + b, 1);
+      mbar_init(aempty + b, EPI_WARPS);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == 1) {  // two accumulators of BN columns in all of TMEM (one CTA per SM)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN)
+                 "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -163,43 +182,59 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // tiles t = blockIdx.x, + gridDim.x, ...: rows of X vary fastest, so the CTAs working at
+  // the same time share W tiles
   if (warp == 0) {
     if (lane == 0) {  // producer
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES && !mbar_wait(empty + s, ((kb / STAGES) - 1) & 1, p.error)) break;
-        unsigned char* a = ring + s * STAGE_BYTES;
-        mbar_arrive_expect_tx(full + s, STAGE_BYTES);
-        tma_load_2d(a, &tmx, full + s, kb * BK, m0);
-        if (SWIGLU) {  // gate rows n0.., then up rows inter + n0..
-          tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
-          tma_load_2d(a + A_BYTES + B_BYTES / 2, &tmw, full + s, kb * BK, p.inter + n0);
-        } else {
-          tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
+      bool ok = true;
+      for (int t = blockIdx.x, it = 0; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t % mt) * BM, n0 = (t / mt) * NOUT;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !(ok = mbar_wait(empty + s, ((it / STAGES) - 1) & 1, p.error))) break;
+          unsigned char* a = ring + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(full + s, STAGE_BYTES);
+          tma_load_2d(a, &tmx, full + s, kb * BK, m0);
+          if (SWIGLU) {  // gate rows n0.., then up rows inter + n0..
+            tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
+            tma_load_2d(a + A_BYTES + B_BYTES / 2, &tmw, full + s, kb * BK, p.inter + n0);
+          } else {
+            tma_load_2d(a + A_BYTES, &tmw, full + s, kb * BK, n0);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(full + s, (kb / STAGES) & 1, p.error)) break;
+    if (lane == 0) {  // MMA issuer: tile lt accumulates into TMEM columns (lt & 1) * BN ..
+      bool ok = true;
+      for (int t = blockIdx.x, it = 0, lt = 0; t < tiles && ok; t += gridDim.x, ++lt) {
+        const int b = lt & 1, use = lt >> 1;
+        if (use > 0 && !(ok = mbar_wait(aempty + b, (use - 1) & 1, p.error))) break;
         tc_fence_after();
-        const uint32_t a = smem_u32(ring + s * STAGE_BYTES), b = a + A_BYTES;
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!(ok = mbar_wait(full + s, (it / STAGES) & 1, p.error))) break;
+          tc_fence_after();
+          const uint32_t a = smem_u32(ring + s * STAGE_BYTES), bb = a + A_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)  // 16 columns = 32 bytes along the swizzled row
-          umma_bf16(tmem, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) != 0);
-        umma_commit(empty + s);  // frees the stage once these MMAs have read it
+          for (int k = 0; k < BK / 16; ++k)  // 16 columns = 32 bytes along the swizzled row
+            umma_bf16<BN>(d, sdesc_sw128(a + 32 * k), sdesc_sw128(bb + 32 * k), (kb | k) != 0);
+          umma_commit(empty + s);  // frees the stage once these MMAs have read it
+        }
+        umma_commit(afull + b);  // the tile's MMAs are complete (also after a give-up)
       }
-      umma_commit(accum);  // all issued MMAs complete (also on the error path)
     }
-  } else {  // epilogue: warps 2-5 read TMEM lanes 32 * (warp % 4) .. + 31
-    const int q = warp & 3;
-    if (mbar_wait(accum, 0, p.error)) {
+  } else {  // epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31, columns of half (w - 2) / 4
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    constexpr int NH = NOUT / 2;
+    for (int t = blockIdx.x, lt = 0; t < tiles; t += gridDim.x, ++lt) {
+      const int b = lt & 1, use = lt >> 1;
+      if (!mbar_wait(afull + b, use & 1, p.error)) break;
       tc_fence_after();
-      const int row = m0 + 32 * q + lane;
-      const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
-      for (int c0 = 0; c0 < NOUT; c0 += 32) {
+      const int row = (t % mt) * BM + 32 * q + lane, n0 = (t / mt) * NOUT;
+      const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
+      for (int c0 = half * NH; c0 < (half + 1) * NH; c0 += 32) {
         uint32_t w[16];
         if constexpr (SWIGLU) {
           uint32_t g[32], u[32];
@@ -225,13 +260,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (row < p.C && n0 + c0 < p.N) store32(p.Y + (size_t)row * p.ldy + n0 + c0, w, p.N - n0 - c0);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(aempty + b)) : "memory");
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -263,18 +301,49 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, in
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr int kTcGemmSmem = STAGES * STAGE_BYTES + 1024 + 256;
+template <int BN>
+constexpr int smem_bytes() {
+  return STAGES * stage_bytes<BN>() + 1024 + 256;
+}
 
-template <bool SWIGLU>
-cudaError_t set_smem_once() {
-  static int set_dev = -1;
+// Sets the kernel's shared-memory limit once per device; returns the device's SM count.
+template <int BN, bool SWIGLU>
+cudaError_t set_smem_once(int& sms) {
+  static int set_dev = -1, set_sms = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || set_dev == dev) return e;
-  e = cudaFuncSetAttribute((const void*)gemm_tc_kernel<SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kTcGemmSmem);
-  if (e == cudaSuccess) set_dev = dev;
-  return e;
+  if (e != cudaSuccess) return e;
+  if (set_dev != dev) {
+    if ((e = cudaFuncSetAttribute((const void*)gemm_tc_kernel<BN, SWIGLU>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<BN>())) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&set_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    set_dev = dev;
+  }
+  sms = set_sms;
+  return cudaSuccess;
+}
+
+template <int BN, bool SWIGLU>
+cudaError_t launch_tile(cudaStream_t s, const CUtensorMap& mx, const void* W, int wrows, int K, const TcGemmArgs& a,
+                        int tiles) {
+  int sms = 0;
+  cudaError_t e = set_smem_once<BN, SWIGLU>(sms);
+  if (e != cudaSuccess) return e;
+  CUtensorMap mw;
+  if (!make_map(&mw, W, wrows, K, K, SWIGLU ? BN / 2 : BN)) return cudaErrorInvalidValue;
+  CUtensorMap mxc = mx;
+  TcGemmArgs ac = a;
+  void* args[] = {&mxc, &mw, &ac};
+  return launch_with(s, false, dim3(std::min(tiles, sms)), dim3(THREADS), smem_bytes<BN>(),
+                     (const void*)gemm_tc_kernel<BN, SWIGLU>, args);
+}
+
+// The persistent grid's time in units of W rows: tiles per CTA x (tile width + a fixed
+// per-tile cost worth 64 rows, fitted to the measured q|k|v, o, gate|up and down shapes).
+int tile_cost(int C, int N, int BN, int sms) {
+  const int tiles = ((N + BN - 1) / BN) * ((C + BM - 1) / BM);
+  return ((tiles + sms - 1) / sms) * (BN + 64);
 }
 
 }  // namespace
@@ -287,28 +356,34 @@ bool gemm_tc_supported(int C, int N, int K, int ldx, int ldy, const void* X, con
 cudaError_t launch_gemm_tc(cudaStream_t s, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y,
                            int ldy, int C, int32_t* error) {
   if (!gemm_tc_supported(C, N, K, ldx, ldy, X, W, Y)) return cudaErrorInvalidValue;
-  cudaError_t e = set_smem_once<false>();
+  int sms = 0;
+  cudaError_t e = set_smem_once<256, false>(sms);
   if (e != cudaSuccess) return e;
-  CUtensorMap mx, mw;
-  if (!make_map(&mx, X, C, K, ldx, BM) || !make_map(&mw, W, N, K, K, BN)) return cudaErrorInvalidValue;
-  TcGemmArgs a{Y, ldy, C, N, K, 0, error};
-  void* args[] = {&mx, &mw, &a};
-  const dim3 grid((N + BN - 1) / BN, (C + BM - 1) / BM);
-  return launch_with(s, false, grid, dim3(THREADS), kTcGemmSmem, (const void*)gemm_tc_kernel<false>, args);
+  CUtensorMap mx;
+  if (!make_map(&mx, X, C, K, ldx, BM)) return cudaErrorInvalidValue;
+  const TcGemmArgs a{Y, ldy, C, N, K, 0, error};
+  // 256- or 192-row tiles, whichever costs less (ties to the wider tile; 128-row tiles were
+  // slower on every measured shape); YUE2_CUDA_GEMM_BN=128|192|256 forces one
+  int best = tile_cost(C, N, 192, sms) < tile_cost(C, N, 256, sms) ? 192 : 256;
+  static const int forced = [] {
+    const char* v = getenv("YUE2_CUDA_GEMM_BN");
+    return v ? atoi(v) : 0;
+  }();
+  if (forced == 128 || forced == 192 || forced == 256) best = forced;
+  const int tiles = ((N + best - 1) / best) * ((C + BM - 1) / BM);
+  if (best == 128) return launch_tile<128, false>(s, mx, W, N, K, a, tiles);
+  if (best == 192) return launch_tile<192, false>(s, mx, W, N, K, a, tiles);
+  return launch_tile<256, false>(s, mx, W, N, K, a, tiles);
 }
 
 // h[C, I] = bf16(bf16(silu(bf16(X . Wg^T))) * bf16(X . Wu^T)) with Wgu = [Wg; Wu] ([2I, K]).
 cudaError_t launch_gemm_tc_swiglu(cudaStream_t s, const uint16_t* Wgu, int I, int K, const uint16_t* X, int ldx,
                                   uint16_t* H, int ldh, int C, int32_t* error) {
-  if (I % (BN / 2) || !gemm_tc_supported(C, I, K, ldx, ldh, X, Wgu, H)) return cudaErrorInvalidValue;
-  cudaError_t e = set_smem_once<true>();
-  if (e != cudaSuccess) return e;
-  CUtensorMap mx, mw;
-  if (!make_map(&mx, X, C, K, ldx, BM) || !make_map(&mw, Wgu, 2 * I, K, K, BN / 2)) return cudaErrorInvalidValue;
-  TcGemmArgs a{H, ldh, C, I, K, I, error};
-  void* args[] = {&mx, &mw, &a};
-  const dim3 grid(I / (BN / 2), (C + BM - 1) / BM);
-  return launch_with(s, false, grid, dim3(THREADS), kTcGemmSmem, (const void*)gemm_tc_kernel<true>, args);
+  if (I % 128 || !gemm_tc_supported(C, I, K, ldx, ldh, X, Wgu, H)) return cudaErrorInvalidValue;
+  CUtensorMap mx;
+  if (!make_map(&mx, X, C, K, ldx, BM)) return cudaErrorInvalidValue;
+  const TcGemmArgs a{H, ldh, C, I, K, I, error};
+  return launch_tile<256, true>(s, mx, Wgu, 2 * I, K, a, (I / 128) * ((C + BM - 1) / BM));
 }
 
 }  // namespace y2
