@@ -189,7 +189,7 @@ def main():
         return run_reference(args)
 
     import torch
-    from yue2_rs_b200 import Model, Phase, Request, Session, generate_batch, synth, _lib
+    from yue2_rs_b200 import Model, Phase, Request, Sampling, Session, generate_batch, synth, _lib
 
     from yue2_rs_b200.dp import DataParallel
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -328,6 +328,40 @@ def main():
                            "hbm_frac_of_measured": sb / (bms / ks * 1e-3) / 1e9 / peak,
                            "forward": "gemm"}
 
+    # ---- the real vocabulary (184,704 ids) in the Semantic phase: the LM head reads only the
+    # 32,768-row codec window and the stop row (project_phase), a sixth of the full head
+    semantic = {}
+    if not args.no_sweep:
+        import copy
+        cs = copy.copy(cfg)
+        cs.vocab_size = 184704
+        ms_model = Model.synthetic(cs, seed=3, std=0.02, device=local)
+        ks, wu = 24, 4
+        sem = Sampling(1.0, 0.93, 50, 1.0, 50, wu + ks + 1, wu + ks + 1)  # no stop before the end
+        codec_ids = lambda ids: [151853 + (t % 32768) for t in ids]
+        ss = Session(ms_model, [Request(codec_ids(cond[:8]), seed=rank + 11, negative=codec_ids(uncond[:8]), scale=SCALE,
+                                        context_fill=PROMPT - 8)], sem, Phase.SEMANTIC)
+        st = torch.cuda.ExternalStream(ss.cuda_stream)
+        ss.step(wu)
+        ss.sync()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        ss.step(ks)
+        b.record(st)
+        ss.sync()
+        barrier()
+        sms = max_over_ranks(a.elapsed_time(b))
+        ss.close()
+        ms_model.close()
+        ctx = PROMPT + wu + ks / 2.0
+        H = cs.hidden_size
+        sb = weight_bytes(cs) - cs.vocab_size * H * 2 + (32768 + 1) * H * 2 + 2 * kv_bytes_per_token(cs) * ctx
+        semantic = {"vocab": cs.vocab_size, "phase": "semantic (codec window + MUSIC_END)",
+                    "tokens_per_s": world * ks / (sms / 1000.0), "ms_per_step": sms / ks, "context_mid": ctx,
+                    "step_bytes": sb, "hbm_frac_of_measured": sb / (sms / ks * 1e-3) / 1e9 / peak,
+                    "lm_head_bytes_read": (32768 + 1) * H * 2, "lm_head_bytes_full": cs.vocab_size * H * 2}
+
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()
     t0 = time.perf_counter()
@@ -359,6 +393,7 @@ def main():
                           "frac_of_8TBs": step_bytes / (ms / K * 1e-3) / 8e12},
         "ctx_sweep": sweep,
         "batched": batched,
+        "semantic_real_vocab": semantic,
         "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "prefill_seconds": outs[0].prefill_seconds, "library_seconds": outs[0].seconds,
                 "decode_ms": outs[0].decode_ms,
