@@ -362,6 +362,42 @@ def main():
                     "step_bytes": sb, "hbm_frac_of_measured": sb / (sms / ks * 1e-3) / 1e9 / peak,
                     "lm_head_bytes_read": (32768 + 1) * H * 2, "lm_head_bytes_full": cs.vocab_size * H * 2}
 
+    # ---- the NAR flow-matching velocity (Model::velocity) at the reference's largest acoustic
+    # chunk: a 1,024-id prefix, then (CONTEXT - 1,024 - 3) / 2 = 11,774 latent frames whose
+    # codec ids fill the cache, and one velocity call over all frames (non-causal attention
+    # to the prefix, the codec ids and every frame)
+    nar = {}
+    if not args.no_sweep:
+        nm = Model.synthetic(cfg, seed=4, std=0.02, norm_mean=1.0, device=local, nar=True)
+        frames = (24576 - PROMPT - 3) // 2
+        length = PROMPT + frames + 1
+        nc = nm.new_cache(24576)
+        nc.fill_normal(length, seed=rank + 5)
+        st = np.random.default_rng(rank).standard_normal((frames, cfg.latent_dim)).astype(np.float32)
+        st = ((st.view(np.uint32).astype(np.uint64) + 0x7FFF + ((st.view(np.uint32) >> 16) & 1)) &
+              0xFFFF0000).astype(np.uint32).view(np.float32)
+        for _ in range(2):
+            nm.velocity(st, nc, 0.5)
+        reps = 3
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            vel = nm.velocity(st, nc, 0.5)
+        vms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / reps)
+        assert np.isfinite(vel).all()
+        n = frames + 2
+        H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+        qd, kd = cfg.num_attention_heads * D, cfg.num_key_value_heads * D
+        lin = 2.0 * n * cfg.num_hidden_layers * H * (qd + 2 * kd + qd + 3 * I)
+        att = 4.0 * n * (length + n) * cfg.num_attention_heads * D * cfg.num_hidden_layers
+        nc.close()
+        nm.close()
+        nar = {"frames": frames, "prefix_positions": length, "ms_per_velocity": vms,
+               "frames_per_s": world * frames / (vms / 1000.0), "linear_tflop": lin / 1e12,
+               "attention_tflop": att / 1e12, "achieved_tflops": (lin + att) / (vms * 1e-3) / 1e12,
+               "what": "yue2_velocity with host state in / velocity out, 3B-shaped NAR layers (synthetic), "
+                       "one call = every frame through 28 layers; synthesize makes 2 per ODE step"}
+
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()
     t0 = time.perf_counter()
@@ -394,6 +430,7 @@ def main():
         "ctx_sweep": sweep,
         "batched": batched,
         "semantic_real_vocab": semantic,
+        "nar_velocity": nar,
         "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "prefill_seconds": outs[0].prefill_seconds, "library_seconds": outs[0].seconds,
                 "decode_ms": outs[0].decode_ms,

@@ -170,6 +170,12 @@ int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_up
  * `avg_ms` (nullable) gets the mean. */
 int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl, int reps,
                     double* avg_ms);
+/* Reserves device slots for the NAR (flow-matching) tensors of Model::open
+ * (src/model.rs:418-451): latent_pos_embed.pe, vae2llm/llm2vae weight+bias,
+ * time_embedder.mlp.{0,2} weight+bias and every layer's nar_self_attn / nar_mlp /
+ * nar_*layernorm. Call before loading (yue2_model_load_checkpoint or set_tensor), then
+ * yue2_model_finalize, which then also requires these tensors. */
+int yue2_model_enable_nar(Yue2Model* m, uint64_t latent_dim, uint64_t max_latent_frames, float timestep_shift);
 /* Header validation only (no device needed): the number of tensors in the checkpoint. */
 int yue2_checkpoint_scan(const char* dir, uint64_t* tensors);
 /* Copies a device tensor back as bf16 bits (count elements). */
@@ -198,6 +204,15 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
 /* Model::prefill / prefill_phase (src/model.rs:508-522, 592-610): append `n` ids to the
  * cache; logits of the last id (nullable). */
 int yue2_prefill(Yue2Model* m, Yue2Cache* c, const int64_t* ids, uint64_t n, int phase, float* logits);
+
+/* Model::velocity (src/model.rs:611-697, nar_cond_end = 0): the flow-matching velocity of
+ * `rows` latent frames `state` [rows, latent_dim] (host f32 holding bf16 values, as the
+ * solver's states are) at logit time `raw_t`, attending to the whole cache prefix and to
+ * every latent row (no causal mask); `out` [rows, latent_dim] (host). Cache length + rows + 2
+ * within the cache capacity (the latent rows' K/V go to the pages past the length as
+ * scratch); the cache's length does not change. Needs yue2_model_enable_nar and head_dim 64
+ * or 128. */
+int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uint64_t rows, double raw_t, float* out);
 
 /* Request-local MT19937 (src/sampling.rs:10-62), state kept on the device of `m`. */
 int yue2_rng_create(Yue2Model* m, uint64_t seed, Yue2Rng** out);

@@ -58,6 +58,8 @@ _P = {
     "orc_powi": (c_f, [c_f, c_int]),
     "orc_generate": (c_int, [c_p, c_p, c_u64, c_p, c_u64, ctypes.POINTER(OrcSampling), c_u64, c_int, c_f, c_int,
                              c_p, ctypes.POINTER(c_u64), ctypes.POINTER(c_int)]),
+    "orc_model_nar": (c_int, [c_p, c_u64, c_u64, c_f]),
+    "orc_velocity": (c_int, [c_p, c_p, c_p, c_u64, ctypes.c_double, c_p]),
 }
 
 _lib = None
@@ -120,9 +122,12 @@ class OracleModel:
             raise OracleError(lib().orc_last_error().decode())
 
     @classmethod
-    def from_tensors(cls, config, items):
-        """items: iterable of (name, dtype code, shape, array)."""
+    def from_tensors(cls, config, items, nar=False):
+        """items: iterable of (name, dtype code, shape, array). nar: also keep the NAR
+        pathway's tensors (Model::velocity)."""
         m = cls(config)
+        if nar:
+            _ck(lib().orc_model_nar(m._h, config.latent_dim, config.max_latent_frames, config.timestep_shift))
         for name, code, shape, arr in items:
             rows, cols = (shape[0], int(np.prod(shape[1:]))) if len(shape) > 1 else (1, shape[0])
             m.set(name, arr, code, rows, cols)
@@ -166,6 +171,14 @@ class OracleModel:
         ids = np.ascontiguousarray(ids, dtype=np.int64)
         out = np.empty(self.config.vocab_size, dtype=np.float32) if logits else None
         _ck(lib().orc_prefill(self._h, cache._h, _ptr(ids), ids.size, phase, _ptr(out) if logits else None))
+        return out
+
+    def velocity(self, state, cache, raw_t):
+        """Model::velocity (src/model.rs:611-697) with nar_cond_end = 0: state [rows, latent]
+        (bf16-valued f32) -> velocity [rows, latent]. The cache is not changed."""
+        st = np.ascontiguousarray(state, dtype=np.float32)
+        out = np.empty_like(st)
+        _ck(lib().orc_velocity(self._h, cache._h, _ptr(st), st.shape[0], float(raw_t), _ptr(out)))
         return out
 
     def hidden(self, ids, cache):

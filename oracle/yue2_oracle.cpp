@@ -78,6 +78,15 @@ struct Model {
   std::vector<float> final_norm;
   std::vector<Layer> layers;
   bool ready = false;
+  // NAR pathway (model.rs:246-270, 401-451): per-layer nar_* weights (in_norm =
+  // nar_input_layernorm, post_norm = nar_pre_mlp_layernorm), latent projections and the
+  // time embedder; enabled by orc_model_nar
+  bool nar_on = false;
+  size_t latent = 0, max_frames = 0;
+  float shift = 1.f;
+  std::vector<Layer> nar;
+  Matrix pe, vae2llm, llm2vae, time_in, time_out;
+  std::vector<float> vae2llm_b, llm2vae_b, time_in_b, time_out_b;
 };
 
 struct Cache {
@@ -110,8 +119,10 @@ float half_to_float(uint16_t h) {
 // op amplifies a change of f32 summation order (the parity noise floor).
 int g_dot_order = 0;
 
-// y[r, n] = round_bf16(sum_k W[n,k] x[r,k]) -- Linear::apply + finish (tensor.rs:946-1118)
-void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin = 0, size_t end = SIZE_MAX) {
+// y[r, n] = round_bf16(sum_k W[n,k] x[r,k] [+ bias[n]]) -- Linear::apply + finish
+// (tensor.rs:946-1118; the bias, already bf16-rounded, is added before the rounding)
+void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin = 0, size_t end = SIZE_MAX,
+            const std::vector<float>* bias = nullptr) {
   if (end == SIZE_MAX) end = W.rows;
   const size_t K = W.cols, N = end - begin;
 #pragma omp parallel
@@ -126,6 +137,7 @@ void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin
         if (g_dot_order == 1) {
           float s = 0.f;
           for (size_t k = 0; k < K; ++k) s += wrow[k] * xr[k];
+          if (bias) s += (*bias)[begin + n];
           y[r * N + n] = round_bf16(s);
           continue;
         }
@@ -136,6 +148,7 @@ void linear(const Matrix& W, const float* x, size_t rows, float* y, size_t begin
         float s = 0.f;
         for (int l = 0; l < 16; ++l) s += acc[l];
         for (; k < K; ++k) s += wrow[k] * xr[k];
+        if (bias) s += (*bias)[begin + n];
         y[r * N + n] = round_bf16(s);
       }
     }
@@ -205,8 +218,8 @@ void attention(const Config& c, const float* q, size_t rows, const std::vector<f
           for (size_t d = 0; d < c.dim; ++d) s += qr[d] * kr[d];
           scores[j] = s;
         }
-        // softmax_row (tensor.rs:706-724)
-        size_t visible = causal_start + start + r + 1;
+        // softmax_row (tensor.rs:706-724); a causal start past the keys sees every key
+        size_t visible = std::min<size_t>(causal_start + start + r + 1, keys);
         for (size_t j = visible; j < keys; ++j) scores[j] = 0.f;
         float mx = -INFINITY;
         for (size_t j = 0; j < visible; ++j) {
@@ -415,6 +428,33 @@ ORC_API int orc_model_set(void* p, const char* name, int dtype, const void* data
   if (n == "model.norm.weight") return set_norm(m->final_norm, H);
   unsigned li;
   char rest[128];
+  if (m->nar_on) {  // NAR tensors (model.rs:246-270, 428-451)
+    const size_t D = m->latent, F = m->max_frames;
+    if (n == "latent_pos_embed.pe") return set_matrix(m->pe, F, H);
+    if (n == "vae2llm.weight") return set_matrix(m->vae2llm, H, D);
+    if (n == "vae2llm.bias") return set_norm(m->vae2llm_b, H);
+    if (n == "llm2vae.weight") return set_matrix(m->llm2vae, D, H);
+    if (n == "llm2vae.bias") return set_norm(m->llm2vae_b, D);
+    if (n == "time_embedder.mlp.0.weight") return set_matrix(m->time_in, H, 256);
+    if (n == "time_embedder.mlp.0.bias") return set_norm(m->time_in_b, H);
+    if (n == "time_embedder.mlp.2.weight") return set_matrix(m->time_out, H, H);
+    if (n == "time_embedder.mlp.2.bias") return set_norm(m->time_out_b, H);
+    if (sscanf(name, "model.layers.%u.%127s", &li, rest) == 2 && li < c.layers) {
+      Layer& L = m->nar[li];
+      std::string r(rest);
+      if (r == "nar_input_layernorm.weight") return set_norm(L.in_norm, H);
+      if (r == "nar_pre_mlp_layernorm.weight") return set_norm(L.post_norm, H);
+      if (r == "nar_self_attn.q_norm.weight") return set_norm(L.q_norm, c.dim);
+      if (r == "nar_self_attn.k_norm.weight") return set_norm(L.k_norm, c.dim);
+      if (r == "nar_self_attn.q_proj.weight") return set_matrix(L.q, qd, H);
+      if (r == "nar_self_attn.k_proj.weight") return set_matrix(L.k, kd, H);
+      if (r == "nar_self_attn.v_proj.weight") return set_matrix(L.v, kd, H);
+      if (r == "nar_self_attn.o_proj.weight") return set_matrix(L.o, H, qd);
+      if (r == "nar_mlp.gate_proj.weight") return set_matrix(L.gate, c.inter, H);
+      if (r == "nar_mlp.up_proj.weight") return set_matrix(L.up, c.inter, H);
+      if (r == "nar_mlp.down_proj.weight") return set_matrix(L.down, H, c.inter);
+    }
+  }
   if (sscanf(name, "model.layers.%u.%127s", &li, rest) == 2 && li < c.layers) {
     Layer& L = m->layers[li];
     std::string r(rest);
@@ -776,3 +816,94 @@ ORC_API float orc_det_expf(float x) { return det_expf(x); }
 ORC_API double orc_det_log1p(double x) { return det_log1p(x); }
 ORC_API float orc_round_bf16(float x) { return round_bf16(x); }
 ORC_API float orc_powi(float a, int b) { return powi_f32(a, b); }
+
+// ---------------------------------------------------------------- NAR velocity
+// Enables the NAR tensors (Config latent_dim, max_latent_frames, timestep_shift).
+ORC_API int orc_model_nar(void* p, uint64_t latent_dim, uint64_t max_frames, float shift) {
+  Model* m = (Model*)p;
+  if (!latent_dim || !max_frames || !(shift > 0.f)) return fail("Invalid latent configuration");
+  m->nar_on = true;
+  m->latent = latent_dim;
+  m->max_frames = max_frames;
+  m->shift = shift;
+  m->nar.resize(m->c.layers);
+  return 0;
+}
+
+// Model::velocity CPU branch (model.rs:611-697) with nar_cond_end = 0: the latent rows
+// (state, zero-padded by one row on each side) at positions cache.length.. attend to the
+// whole cache prefix and to each other; out = llm2vae(final_norm(x))[1 .. rows + 1].
+ORC_API int orc_velocity(void* mp, void* cp, const float* state, uint64_t rows, double raw_t, float* out) {
+  Model& m = *(Model*)mp;
+  Cache& cache = *(Cache*)cp;
+  const Config& c = m.c;
+  if (!m.nar_on || m.vae2llm.w.empty() || m.llm2vae.w.empty() || m.time_in.w.empty() || m.time_out.w.empty() ||
+      m.pe.w.empty())
+    return fail("NAR tensors missing");
+  for (auto& L : m.nar)
+    if (L.q.w.empty() || L.down.w.empty() || L.in_norm.empty() || L.post_norm.empty() || L.q_norm.empty())
+      return fail("NAR tensors missing");
+  if (cache.key.size() != m.layers.size()) return fail("cache/model mismatch");
+  const size_t n = rows + 2, H = c.hidden, D = m.latent, qd = c.heads * c.dim, kd = c.kv * c.dim;
+  std::vector<float> padded(n * D, 0.f), x(n * H);
+  for (size_t i = 0; i < rows * D; ++i) padded[D + i] = state[i];
+  linear(m.vae2llm, padded.data(), n, x.data(), 0, SIZE_MAX, &m.vae2llm_b);
+  // timestep embedding (f32 math in the reference's order)
+  const float raw = round_bf16((float)raw_t);
+  const float sig = round_bf16(1.0f / (1.0f + expf(-raw)));
+  const float top = round_bf16(m.shift * sig);
+  const float bottom = round_bf16(1.f + round_bf16((m.shift - 1.f) * sig));
+  const float t = round_bf16(top / bottom);
+  std::vector<float> sinus(256), time(H), time2(H);
+  for (int i = 0; i < 128; ++i) {
+    const float f = expf(-logf(10000.f) * (float)i / 128.f);
+    sinus[i] = round_bf16(cosf(t * f));
+    sinus[128 + i] = round_bf16(sinf(t * f));
+  }
+  linear(m.time_in, sinus.data(), 1, time.data(), 0, SIZE_MAX, &m.time_in_b);
+  for (auto& v : time) v = round_bf16(v / (1.0f + expf(-v)));
+  linear(m.time_out, time.data(), 1, time2.data(), 0, SIZE_MAX, &m.time_out_b);
+  for (size_t r = 0; r < n; ++r)
+    for (size_t i = 0; i < H; ++i) {
+      const float pe = round_bf16(bf(m.pe.w[std::min(r, m.max_frames - 1) * H + i]));
+      float& v = x[r * H + i];
+      v = round_bf16(round_bf16(v + time2[i]) + pe);
+    }
+  const size_t visible = cache.length;
+  Rotary rot(cache.length, n, c);
+  std::vector<float> h(n * H), q(n * qd), k(n * kd), v(n * kd), att(n * qd), proj(n * H);
+  std::vector<float> gate(n * c.inter), up(n * c.inter);
+  for (size_t li = 0; li < m.nar.size(); ++li) {
+    Layer& L = m.nar[li];
+    norm_rows(L.in_norm, c.eps, x.data(), n, H, h.data());
+    linear(L.q, h.data(), n, q.data());
+    linear(L.k, h.data(), n, k.data());
+    linear(L.v, h.data(), n, v.data());
+    norm_rows(L.q_norm, c.eps, q.data(), n * c.heads, c.dim, q.data());
+    norm_rows(L.k_norm, c.eps, k.data(), n * c.kv, c.dim, k.data());
+    rot.apply(q.data(), qd);
+    rot.apply(k.data(), kd);
+    std::vector<float> key(cache.key[li].begin(), cache.key[li].begin() + visible * kd);
+    std::vector<float> value(cache.value[li].begin(), cache.value[li].begin() + visible * kd);
+    key.insert(key.end(), k.begin(), k.end());
+    value.insert(value.end(), v.begin(), v.end());
+    attention(c, q.data(), n, key, value, visible + n, visible + n, att.data());  // no causal mask
+    linear(L.o, att.data(), n, proj.data());
+    for (size_t i = 0; i < n * H; ++i) x[i] = round_bf16(x[i] + proj[i]);
+    norm_rows(L.post_norm, c.eps, x.data(), n, H, h.data());
+    linear(L.gate, h.data(), n, gate.data());
+    linear(L.up, h.data(), n, up.data());
+    for (size_t i = 0; i < n * c.inter; ++i) {
+      float g = gate[i];
+      g = round_bf16(g / (1.0f + expf(-g)));
+      gate[i] = round_bf16(g * up[i]);
+    }
+    linear(L.down, gate.data(), n, proj.data());
+    for (size_t i = 0; i < n * H; ++i) x[i] = round_bf16(x[i] + proj[i]);
+  }
+  std::vector<float> fin(n * H), lat(n * D);
+  norm_rows(m.final_norm, c.eps, x.data(), n, H, fin.data());
+  linear(m.llm2vae, fin.data(), n, lat.data(), 0, SIZE_MAX, &m.llm2vae_b);
+  for (size_t i = 0; i < rows * D; ++i) out[i] = lat[D + i];
+  return 0;
+}

@@ -90,6 +90,7 @@ _PROTOS = {
     "yue2_model_init_synthetic": (c_int, [c_p, c_u64, c_f, c_f]),
     "yue2_model_finalize": (c_int, [c_p]),
     "yue2_model_load_checkpoint": (c_int, [c_p, ctypes.c_char_p, ctypes.POINTER(c_u64)]),
+    "yue2_model_enable_nar": (c_int, [c_p, c_u64, c_u64, c_f]),
     "yue2_checkpoint_scan": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_u64)]),
     "yue2_bench_gemm": (c_int, [c_p, c_p, c_p, c_p, c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
     "yue2_model_get_tensor": (c_int, [c_p, ctypes.c_char_p, c_p, c_u64]),
@@ -101,6 +102,7 @@ _PROTOS = {
     "yue2_cache_read": (c_int, [c_p, c_u64, c_u64, c_u64, c_p, c_p]),
     "yue2_forward": (c_int, [c_p, c_p, c_p, c_u64, c_int, c_p]),
     "yue2_prefill": (c_int, [c_p, c_p, c_p, c_u64, c_int, c_p]),
+    "yue2_velocity": (c_int, [c_p, c_p, c_p, c_u64, ctypes.c_double, c_p]),
     "yue2_rng_create": (c_int, [c_p, c_u64, ctypes.POINTER(c_p)]),
     "yue2_rng_free": (None, [c_p]),
     "yue2_rng_state": (c_int, [c_p, c_p, ctypes.POINTER(c_u64)]),

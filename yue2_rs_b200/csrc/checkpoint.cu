@@ -422,7 +422,7 @@ int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_up
     const uint64_t cols = e.shape.size() > 1 ? e.count / std::max<uint64_t>(1, e.shape[0]) : e.count;
     if (e.count != t.rows * t.cols || (!t.norm && (rows != t.rows || cols != t.cols)))
       return fail(YUE2_ERR_INVALID, "Tensor shape mismatch for " + kv.first);
-    void* dst = m->arena + t.offset;
+    void* dst = m->slot_addr(t);
     // put() copies its source into pinned memory before it returns, so the host vectors
     // below may be refilled for the next tensor at once
     if (t.norm) {  // Norm::new: gains rounded to bf16 (src/tensor.rs:1126-1136), f32 on the device

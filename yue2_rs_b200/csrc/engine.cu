@@ -288,6 +288,95 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   return 0;
 }
 
+// Model::open's NAR tensors (src/model.rs:246-270, 428-451), in an allocation of their own.
+int yue2_model_enable_nar(Yue2Model* m, uint64_t latent_dim, uint64_t max_latent_frames, float timestep_shift) {
+  if (!m) return fail(YUE2_ERR_INVALID, "null model");
+  if (m->nar_arena) return fail(YUE2_ERR_INVALID, "NAR tensors already enabled");
+  // Config::read validation (src/model.rs:50-72)
+  if (!latent_dim || latent_dim % 8 || latent_dim > 4096 || !max_latent_frames || !(timestep_shift > 0.f) ||
+      !std::isfinite(timestep_shift))
+    return fail(YUE2_ERR_INVALID, "Invalid latent configuration (latent_dim a multiple of 8)");
+  int rc = y2_set_device(m);
+  if (rc) return rc;
+  const Geometry& g = m->g;
+  const size_t H = g.hidden, I = g.inter, D = g.dim, L = latent_dim, F = max_latent_frames;
+  const size_t qd = (size_t)g.heads * D, kd = (size_t)g.kvh * D;
+  auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  size_t total = 0;
+  std::vector<std::pair<std::string, TensorSlot>> plan;
+  auto add = [&](const std::string& name, size_t rows, size_t cols, bool norm) {
+    TensorSlot t;
+    t.rows = rows;
+    t.cols = cols;
+    t.norm = norm;
+    t.offset = total;
+    total += al(rows * cols * (norm ? 4 : 2));
+    plan.push_back({name, t});
+  };
+  add("latent_pos_embed.pe", F, H, false);
+  add("vae2llm.weight", H, L, false);
+  add("vae2llm.bias", 1, H, true);
+  add("llm2vae.weight", L, H, false);
+  add("llm2vae.bias", 1, L, true);
+  add("time_embedder.mlp.0.weight", H, 256, false);
+  add("time_embedder.mlp.0.bias", 1, H, true);
+  add("time_embedder.mlp.2.weight", H, H, false);
+  add("time_embedder.mlp.2.bias", 1, H, true);
+  for (int l = 0; l < g.layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    add(p + "nar_self_attn.q_proj.weight", qd, H, false);
+    add(p + "nar_self_attn.k_proj.weight", kd, H, false);
+    add(p + "nar_self_attn.v_proj.weight", kd, H, false);
+    add(p + "nar_self_attn.o_proj.weight", H, qd, false);
+    add(p + "nar_mlp.gate_proj.weight", I, H, false);
+    add(p + "nar_mlp.up_proj.weight", I, H, false);
+    add(p + "nar_mlp.down_proj.weight", H, I, false);
+    add(p + "nar_input_layernorm.weight", 1, H, true);
+    add(p + "nar_self_attn.q_norm.weight", 1, D, true);
+    add(p + "nar_self_attn.k_norm.weight", 1, D, true);
+    add(p + "nar_pre_mlp_layernorm.weight", 1, H, true);
+  }
+  void* arena = nullptr;
+  if ((rc = m->alloc(&arena, total))) return rc;
+  m->nar_arena = (char*)arena;
+  for (auto& kv : plan) {
+    kv.second.base = m->nar_arena;
+    m->slots[kv.first] = kv.second;
+  }
+  auto ptr = [&](const std::string& n) { return (void*)(m->nar_arena + m->slots[n].offset); };
+  auto& W = m->nar;
+  W.pe = (uint16_t*)ptr("latent_pos_embed.pe");
+  W.vae2llm = (uint16_t*)ptr("vae2llm.weight");
+  W.vae2llm_b = (float*)ptr("vae2llm.bias");
+  W.llm2vae = (uint16_t*)ptr("llm2vae.weight");
+  W.llm2vae_b = (float*)ptr("llm2vae.bias");
+  W.time_in = (uint16_t*)ptr("time_embedder.mlp.0.weight");
+  W.time_in_b = (float*)ptr("time_embedder.mlp.0.bias");
+  W.time_out = (uint16_t*)ptr("time_embedder.mlp.2.weight");
+  W.time_out_b = (float*)ptr("time_embedder.mlp.2.bias");
+  W.latent = (int)L;
+  W.max_frames = (int)F;
+  W.shift = timestep_shift;
+  m->nar_layers.resize(g.layers);
+  for (int l = 0; l < g.layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    LayerW& w = m->nar_layers[l];
+    w.q = (uint16_t*)ptr(p + "nar_self_attn.q_proj.weight");
+    w.k = (uint16_t*)ptr(p + "nar_self_attn.k_proj.weight");
+    w.v = (uint16_t*)ptr(p + "nar_self_attn.v_proj.weight");
+    w.o = (uint16_t*)ptr(p + "nar_self_attn.o_proj.weight");
+    w.gate = (uint16_t*)ptr(p + "nar_mlp.gate_proj.weight");
+    w.up = (uint16_t*)ptr(p + "nar_mlp.up_proj.weight");
+    w.down = (uint16_t*)ptr(p + "nar_mlp.down_proj.weight");
+    w.in_norm = (float*)ptr(p + "nar_input_layernorm.weight");
+    w.q_norm = (float*)ptr(p + "nar_self_attn.q_norm.weight");
+    w.k_norm = (float*)ptr(p + "nar_self_attn.k_norm.weight");
+    w.post_norm = (float*)ptr(p + "nar_pre_mlp_layernorm.weight");
+  }
+  m->finalized = false;
+  return 0;
+}
+
 int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void* data, uint64_t rows,
                           uint64_t cols) {
   if (!m || !name || !data) return fail(YUE2_ERR_INVALID, "null argument");
@@ -300,7 +389,7 @@ int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void*
     return fail(YUE2_ERR_INVALID, std::string("Tensor shape mismatch for ") + name);
   int rc = y2_set_device(m);
   if (rc) return rc;
-  void* dst = m->arena + t.offset;
+  void* dst = m->slot_addr(t);
   if (t.norm) {  // Norm::new: values rounded to bf16 (tensor.rs:1126-1136)
     std::vector<float> v(count);
     for (size_t i = 0; i < count; ++i) v[i] = round_bf16(host_value(dtype, data, i));
@@ -337,9 +426,9 @@ int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float stddev, float n
         v[i] = round_bf16(norm_mean + stddev * (float)(rad * cos(6.283185307179586 * u2)));
         if (i + 1 < v.size()) v[i + 1] = round_bf16(norm_mean + stddev * (float)(rad * sin(6.283185307179586 * u2)));
       }
-      CK(cudaMemcpy(m->arena + t.offset, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(m->slot_addr(t), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
     } else {
-      CK(launch_fill_normal_bf16(m->stream, (uint16_t*)(m->arena + t.offset), t.rows * t.cols, tseed, 0.f,
+      CK(launch_fill_normal_bf16(m->stream, (uint16_t*)m->slot_addr(t), t.rows * t.cols, tseed, 0.f,
                                  stddev));
     }
     m->loaded.insert(kv.first);
@@ -359,10 +448,10 @@ int yue2_model_get_tensor(Yue2Model* m, const char* name, uint16_t* out, uint64_
   if (rc) return rc;
   if (t.norm) {
     std::vector<float> v(count);
-    CK(cudaMemcpy(v.data(), m->arena + t.offset, count * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(v.data(), m->slot_addr(t), count * 4, cudaMemcpyDeviceToHost));
     for (size_t i = 0; i < count; ++i) out[i] = f32_to_bf16_bits(v[i]);
   } else {
-    CK(cudaMemcpy(out, m->arena + t.offset, count * 2, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(out, m->slot_addr(t), count * 2, cudaMemcpyDeviceToHost));
   }
   return 0;
 }

@@ -26,7 +26,8 @@ struct PagePool {
 
 struct TensorSlot {
   size_t offset = 0, rows = 0, cols = 0;
-  bool norm = false;  // f32 gain vector; matrices are bf16
+  bool norm = false;      // f32 gain (or bias) vector; matrices are bf16
+  char* base = nullptr;   // allocation holding the tensor (null: the model's weight arena)
 };
 
 int fail(int code, const std::string& msg);
@@ -72,6 +73,17 @@ struct Yue2Model {
   uint16_t *embed = nullptr, *lm_head = nullptr;
   float* final_norm = nullptr;
   std::vector<y2::LayerW> layers;
+  // NAR pathway (Model::velocity, src/model.rs:611-697), after yue2_model_enable_nar: the
+  // nar_* layer weights (in_norm = nar_input_layernorm, post_norm = nar_pre_mlp_layernorm),
+  // the latent projections with their bf16-rounded biases and the time embedder
+  struct NarW {
+    const uint16_t *pe = nullptr, *vae2llm = nullptr, *llm2vae = nullptr, *time_in = nullptr, *time_out = nullptr;
+    const float *vae2llm_b = nullptr, *llm2vae_b = nullptr, *time_in_b = nullptr, *time_out_b = nullptr;
+    int latent = 0, max_frames = 0;
+    float shift = 1.f;
+  } nar;
+  std::vector<y2::LayerW> nar_layers;
+  char* nar_arena = nullptr;
 
   float *cos_tab = nullptr, *sin_tab = nullptr;
   int max_pos = 0;
@@ -104,6 +116,7 @@ struct Yue2Model {
   std::map<void*, size_t> scratch_cap;
 
   int alloc(void** p, size_t bytes);
+  char* slot_addr(const y2::TensorSlot& t) const { return (t.base ? t.base : arena) + t.offset; }
   int scratch_take(void** p, size_t bytes);
   void scratch_give(void* p);
   int max_pos_limit() const {

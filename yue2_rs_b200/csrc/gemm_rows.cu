@@ -144,7 +144,7 @@ struct PrefillBufs {
   cublasLtHandle_t lt = nullptr;
   void* ws = nullptr;
   size_t ws_bytes = 0;
-  std::map<std::array<int, 5>, LtGemm> gemms;
+  std::map<std::array<int, 6>, LtGemm> gemms;
 };
 
 void free_prefill(PrefillBufs* p) {
@@ -215,8 +215,8 @@ static int ensure_prefill(Yue2Model& m) {
 // separate pass (YUE2_CUDA_GEMM_SPLITK=1; default: no split), never with in-place or
 // output-type partial sums, so a row's result depends only on the shapes and repeats
 // bit for bit.
-static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
-                   int C);
+static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, void* Y, int ldy,
+                   int C, bool f32out = false);
 
 static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
                      int C) {
@@ -227,10 +227,11 @@ static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16
   return gemm_lt(m, W, N, K, X, ldx, Y, ldy, C);
 }
 
-static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
-                   int C) {
+// f32out: Y is f32 (the unrounded sums, for the biased linears of the NAR pathway).
+static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, void* Y, int ldy,
+                   int C, bool f32out) {
   PrefillBufs& P = *m.prefill;
-  const std::array<int, 5> key = {N, K, ldx, ldy, C};
+  const std::array<int, 6> key = {N, K, ldx, ldy, C, f32out ? 1 : 0};
   auto it = P.gemms.find(key);
   if (it == P.gemms.end()) {
     LtGemm gm;
@@ -241,7 +242,7 @@ static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t
         (st = cublasLtMatmulDescSetAttribute(gm.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb))) ||
         (st = cublasLtMatrixLayoutCreate(&gm.a, CUDA_R_16BF, K, N, K)) ||
         (st = cublasLtMatrixLayoutCreate(&gm.b, CUDA_R_16BF, K, C, ldx)) ||
-        (st = cublasLtMatrixLayoutCreate(&gm.d, CUDA_R_16BF, N, C, ldy)))
+        (st = cublasLtMatrixLayoutCreate(&gm.d, f32out ? CUDA_R_32F : CUDA_R_16BF, N, C, ldy)))
       return lt_fail(st, "cuBLASLt descriptor");
     cublasLtMatmulPreference_t pref = nullptr;
     const uint32_t no_split = m.gemm_split_k ? (uint32_t)CUBLASLT_REDUCTION_SCHEME_COMPUTE_TYPE
@@ -356,13 +357,17 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, DevRow* rows, int l, int 
 }
 
 // ------------------------------------------------------------------ the layers over R rows
-// Layers of R rows whose embeddings are in P.x (f32), ending with the last residual added
-// (the final norm is the caller's). Prefill chunk rows (decode = false) belong to one
+// Layers `lw` of R rows whose embeddings are in P.x (f32), ending with the last residual
+// added (the final norm is the caller's). Prefill chunk rows (decode = false) belong to one
 // cache at positions pos0 + r: rope_append writes all their K/V, then the causal prefill
 // attention runs. Decode rows (decode = true) each have their own cache: the decode
 // attention kernel applies the QK norm and RoPE and appends each row's K/V itself.
-static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const uint64_t* pages, int pos0) {
-  PrefillBufs& P = *m.prefill;
+// causal = false (the NAR pathway's latent rows): every chunk row sees every key up to the
+// chunk's last position.
+static int encode_layers(Yue2Model& m, PrefillBufs& P, const std::vector<LayerW>& lw, DevRow* rows, int R,
+                         bool decode, const uint64_t* pages, int pos0, bool causal = true) {
+  if (!causal && (decode || !prefill_attention_supported(m.g)))
+    return fail(YUE2_ERR_INVALID, "non-causal rows need the tensor-core prefill attention (head_dim 64 or 128)");
   const Geometry& g = m.g;
   const int H = g.hidden, qd = g.heads * g.dim, kd = g.kvh * g.dim, I = g.inter;
   cudaStream_t s = m.stream;
@@ -370,7 +375,7 @@ static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const u
   // one wave of attention CTAs where R is small; the partials hold cap rows x kvh
   const int splits = std::max(1, std::min(std::min(m.max_splits, P.cap / R), 2 * m.sms / (g.kvh * R)));
   for (int l = 0; l < g.layers; ++l) {
-    const LayerW& w = m.layers[l];
+    const LayerW& w = lw[l];
     CK(launch_residual_norm(s, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, R));
     {
       const uint16_t* W[3] = {w.q, w.k, w.v};
@@ -393,7 +398,7 @@ static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const u
       rp.max_pos = m.max_pos;
       rp.error = m.flags + 1;
       CK(launch_rope_append(s, false, rp, R));
-      if (m.prefill_tc_attn && prefill_attention_supported(g)) {
+      if ((m.prefill_tc_attn || !causal) && prefill_attention_supported(g)) {
         PrefillAttnParams fp = {};
         fp.pages = pages;
         fp.q = P.q;
@@ -403,6 +408,7 @@ static int encode_layers(Yue2Model& m, DevRow* rows, int R, bool decode, const u
         fp.C = R;
         fp.pos0 = pos0;
         fp.scale = 1.0f / sqrtf((float)g.dim);
+        fp.causal = causal ? 1 : 0;
         CK(launch_prefill_attention(s, fp));
       } else if ((rc = row_attention(m, P, rows, l, R, splits, false))) {
         return rc;
@@ -446,7 +452,7 @@ static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint6
     CK(launch_with(s, false, dim3((C + 127) / 128), dim3(128), 0, (const void*)prefill_rows_kernel, args));
   }
   CK(launch_embed(s, false, P.rows, C, m.embed, g.hidden, g.vocab, P.x, m.flags + 0));
-  const int rc = encode_layers(m, P.rows, C, false, c.d_pages, (int)(L0 + start));
+  const int rc = encode_layers(m, P, m.layers, P.rows, C, false, c.d_pages, (int)(L0 + start));
   if (rc) return rc;
   // the last layer's residual (the LM head applies the final norm itself)
   CK(launch_residual_norm(s, P.x, P.y, nullptr, g.hidden, g.eps, nullptr, C));
@@ -536,7 +542,7 @@ int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase) {
   const Geometry& g = m.g;
   const int H = g.hidden, V = g.vocab;
   CK(launch_embed(s, false, m.wide_rows, R, m.embed, H, V, P.x, m.flags + 0));
-  if ((rc = encode_layers(m, m.wide_rows, R, true, nullptr, 0))) return rc;
+  if ((rc = encode_layers(m, *m.prefill, m.layers, m.wide_rows, R, true, nullptr, 0))) return rc;
   CK(launch_residual_norm(s, P.x, P.y, m.final_norm, H, g.eps, P.xb, R));
   int lo, hi, start, end, stop;
   head_span(m, phase, lo, hi, start, end, stop);
@@ -583,6 +589,179 @@ int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, i
 }
 
 }  // namespace y2
+
+// ---------------------------------------------------------------- NAR velocity
+namespace y2 {
+
+// v = bf16(y + bias) (Linear::finish with a bf16 bias, src/tensor.rs:1102-1118), then with
+// `silu` v = bf16(silu(v)) (the time embedder's activation, src/model.rs:635-638); into
+// f32 and/or bf16 outputs.
+__global__ void bias_round_kernel(const float* __restrict__ y, const float* __restrict__ bias, int rows, int N,
+                                  int silu, float* __restrict__ outf, uint16_t* __restrict__ outb) {
+  const size_t total = (size_t)rows * N;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    float v = round_bf16(y[i] + bias[i % N]);
+    if (silu) v = round_bf16(v / (1.0f + det_expf(-v)));
+    if (outf) outf[i] = v;
+    if (outb) outb[i] = f2bf_exact(v);
+  }
+}
+
+// x[r] = bf16(bf16(bf16(vae2llm(padded)[r] + bias) + time) + pe[min(r, frames - 1)])
+// (src/model.rs:623-649)
+__global__ void nar_embed_kernel(const float* __restrict__ y, const float* __restrict__ bias,
+                                 const float* __restrict__ time, const uint16_t* __restrict__ pe, int frames, int n,
+                                 int H, float* __restrict__ x) {
+  const size_t total = (size_t)n * H;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / H), c = (int)(i - (size_t)r * H);
+    const float v = round_bf16(y[i] + bias[c]);
+    x[i] = round_bf16(round_bf16(v + time[c]) + bf2f(pe[(size_t)min(r, frames - 1) * H + c]));
+  }
+}
+
+// One device block for a velocity call of n rows: the layer activations (a PrefillBufs of
+// capacity n; the attention partials and counters stay unused, as the non-causal rows take
+// the tensor-core attention) and the NAR inputs and outputs. Taken from the model's scratch
+// and given back when the call ends, so one song's repeated calls reuse it.
+struct NarBufs {
+  PrefillBufs act;
+  uint16_t *lat_in = nullptr, *sinus = nullptr, *time_bf = nullptr;
+  float *yf = nullptr, *time2 = nullptr, *lat_out = nullptr;
+  void* block = nullptr;
+};
+
+static int take_nar(Yue2Model& m, int n, NarBufs& B) {
+  const Geometry& g = m.g;
+  const size_t C = n, H = g.hidden, qd = (size_t)g.heads * g.dim, kd = (size_t)g.kvh * g.dim, I = g.inter;
+  const size_t L = m.nar.latent;
+  size_t off = 0;
+  std::vector<std::pair<void**, size_t>> plan;
+  auto at = [&](void** p, size_t bytes) {
+    plan.push_back({p, off});
+    off += (bytes + 255) & ~(size_t)255;
+  };
+  PrefillBufs& P = B.act;
+  at((void**)&P.x, C * H * 4);
+  at((void**)&P.xb, C * H * 2);
+  at((void**)&P.qkv, C * (qd + 2 * kd) * 2);
+  at((void**)&P.q, C * qd * 2);
+  at((void**)&P.attn, C * qd * 2);
+  at((void**)&P.y, C * H * 2);
+  at((void**)&P.gu, C * 2 * I * 2);
+  at((void**)&P.h, C * I * 2);
+  at((void**)&P.rows, C * sizeof(DevRow));
+  at((void**)&B.lat_in, C * L * 2);
+  at((void**)&B.yf, C * std::max(H, L) * 4);
+  at((void**)&B.lat_out, C * L * 4);
+  at((void**)&B.sinus, 256 * 2);
+  at((void**)&B.time_bf, H * 2);
+  at((void**)&B.time2, H * 4);
+  const int rc = m.scratch_take(&B.block, off);
+  if (rc) return rc;
+  for (auto& p : plan) *p.first = (char*)B.block + p.second;
+  P.cap = n;
+  return 0;
+}
+
+static cudaError_t launch_bias_round(cudaStream_t s, const float* y, const float* bias, int rows, int N, int silu,
+                                     float* outf, uint16_t* outb, int sms) {
+  void* args[] = {&y, &bias, &rows, &N, &silu, &outf, &outb};
+  const int blocks = std::max(1, std::min(4 * sms, (int)(((size_t)rows * N + 255) / 256)));
+  return launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)bias_round_kernel, args);
+}
+
+// The body of yue2_velocity over the buffers B (rows + 2 rows).
+static int velocity_rows(Yue2Model* m, Yue2Cache* c, NarBufs& B, const float* state, uint64_t rows, double raw_t,
+                         float* out) {
+  const Geometry& g = m->g;
+  const uint64_t n = rows + 2;
+  PrefillBufs& P = B.act;
+  int rc;
+  const auto& W = m->nar;
+  const int H = g.hidden, L = W.latent, N = (int)n;
+  cudaStream_t s = m->stream;
+  // host: zero-padded latent rows and the timestep's sinusoidal features (f32 math in the
+  // reference's order, src/model.rs:624-634)
+  std::vector<uint16_t> padded((size_t)n * L, 0);
+  for (size_t i = 0; i < rows * (size_t)L; ++i) padded[L + i] = (uint16_t)(det_f2u(round_bf16(state[i])) >> 16);
+  const float raw = round_bf16((float)raw_t);
+  const float sig = round_bf16(1.0f / (1.0f + expf(-raw)));
+  const float top = round_bf16(W.shift * sig);
+  const float bottom = round_bf16(1.f + round_bf16((W.shift - 1.f) * sig));
+  const float t = round_bf16(top / bottom);
+  std::vector<uint16_t> sinus(256);
+  for (int i = 0; i < 128; ++i) {
+    const float f = expf(-logf(10000.f) * (float)i / 128.f);
+    sinus[i] = (uint16_t)(det_f2u(round_bf16(cosf(t * f))) >> 16);
+    sinus[128 + i] = (uint16_t)(det_f2u(round_bf16(sinf(t * f))) >> 16);
+  }
+  CK(cudaMemcpyAsync(B.lat_in, padded.data(), padded.size() * 2, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(B.sinus, sinus.data(), 512, cudaMemcpyHostToDevice, s));
+  // time embedder: time_out(bf16(silu(time_in(sinus))))
+  if ((rc = gemm_lt(*m, W.time_in, H, 256, B.sinus, 256, B.yf, H, 1, true))) return rc;
+  CK(launch_bias_round(s, B.yf, W.time_in_b, 1, H, 1, nullptr, B.time_bf, m->sms));
+  if ((rc = gemm_lt(*m, W.time_out, H, H, B.time_bf, H, B.yf, H, 1, true))) return rc;
+  CK(launch_bias_round(s, B.yf, W.time_out_b, 1, H, 0, B.time2, nullptr, m->sms));
+  // latent rows into the hidden width, plus time and position
+  if ((rc = gemm_lt(*m, W.vae2llm, H, L, B.lat_in, L, B.yf, H, N, true))) return rc;
+  {
+    const float *y = B.yf, *bias = W.vae2llm_b, *time = B.time2;
+    const uint16_t* pe = W.pe;
+    int frames = W.max_frames, nn = N, hh = H;
+    float* x = P.x;
+    void* args[] = {&y, &bias, &time, &pe, &frames, &nn, &hh, &x};
+    const int blocks = std::min(4 * m->sms, (int)(((size_t)N * H + 255) / 256));
+    CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)nar_embed_kernel, args));
+  }
+  {
+    DevRow* dr = P.rows;
+    const uint64_t* pages = c->d_pages;
+    const int32_t* none = nullptr;
+    int32_t pb = 0, pe = 0, p0 = (int32_t)c->length;
+    int nn = N;
+    void* args[] = {&dr, &nn, &pages, &none, &pb, &pe, &p0};
+    CK(launch_with(s, false, dim3((N + 127) / 128), dim3(128), 0, (const void*)prefill_rows_kernel, args));
+  }
+  if ((rc = encode_layers(*m, P, m->nar_layers, P.rows, N, false, c->d_pages, (int)c->length, false))) return rc;
+  CK(launch_residual_norm(s, P.x, P.y, m->final_norm, H, g.eps, P.xb, N));
+  if ((rc = gemm_lt(*m, W.llm2vae, L, H, P.xb, H, B.yf, L, N, true))) return rc;
+  CK(launch_bias_round(s, B.yf, W.llm2vae_b, N, L, 0, B.lat_out, nullptr, m->sms));
+  CK(cudaMemcpyAsync(out, B.lat_out + L, rows * (size_t)L * 4, cudaMemcpyDeviceToHost, s));
+  if ((rc = take_flags(*m))) return rc;
+  CK(cudaStreamSynchronize(s));
+  return 0;
+}
+
+}  // namespace y2
+
+// Model::velocity (src/model.rs:611-697) with nar_cond_end = 0, on the device. The latent
+// rows take positions cache.length .. + rows + 1: their K/V go into the cache's pages past
+// its length (scratch; the length does not change), and every latent row attends to the
+// whole prefix and to every latent row.
+extern "C" int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uint64_t rows, double raw_t,
+                             float* out) {
+  using namespace y2;
+  if (!m || !c || !state || !out) return fail(YUE2_ERR_INVALID, "null argument");
+  if (!m->finalized) return fail(YUE2_ERR_INVALID, "model not finalized");
+  if (!m->nar_arena) return fail(YUE2_ERR_INVALID, "NAR tensors not enabled (yue2_model_enable_nar)");
+  if (c->m != m) return fail(YUE2_ERR_INVALID, "cache belongs to another model");
+  const Geometry& g = m->g;
+  const uint64_t n = rows + 2;
+  if (rows == 0) return fail(YUE2_ERR_INVALID, "velocity needs at least one latent row");
+  if (c->length + n > c->capacity || c->length + n > (uint64_t)m->max_pos)
+    return fail(YUE2_ERR_CAPACITY, "latent rows exceed the cache/model context");
+  if (!prefill_attention_supported(g)) return fail(YUE2_ERR_INVALID, "NAR velocity needs head_dim 64 or 128");
+  int rc = y2_set_device(m);
+  if (rc) return rc;
+  if ((rc = ensure_prefill(*m))) return rc;  // the cuBLASLt state the GEMMs share
+  NarBufs B;
+  if ((rc = take_nar(*m, (int)n, B))) return rc;
+  rc = velocity_rows(m, c, B, state, rows, raw_t, out);
+  if (rc) cudaStreamSynchronize(m->stream);  // nothing queued may still use the block
+  m->scratch_give(B.block);
+  return rc;
+}
 
 // ---------------------------------------------------------------- GEMM timing and parity hook
 extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl,

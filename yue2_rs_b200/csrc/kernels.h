@@ -100,6 +100,7 @@ struct PrefillAttnParams {
   Geometry g;
   int layer, C, pos0;
   float scale;
+  int causal;  // 1: row r sees keys up to pos0 + r; 0: every row sees keys up to pos0 + C - 1
 };
 
 struct RopeParams {

@@ -44,7 +44,9 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnP
   const int row0 = tile * kRowsPerCta;
   const int nrows = min(kRowsPerCta, p.C - row0);
   const int q0 = p.pos0 + row0;              // position of the tile's first row
-  const int last_key = q0 + nrows - 1;       // position of its last row
+  // causal: the tile's last row; otherwise (every row sees every row of the chunk) the
+  // chunk's last row
+  const int last_key = p.causal ? q0 + nrows - 1 : p.pos0 + p.C - 1;
   const int nkt = (last_key >> kPageLog2) + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = g.heads * D;
@@ -74,7 +76,9 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnP
   // per-thread rows of the warp's 16: g8 = lane / 4 and g8 + 8; columns 2 * (lane % 4) + {0, 1}
   const int g8 = lane >> 2, t4 = lane & 3;
   const int wrow = warp * 16;
-  const int pos_a = q0 + wrow + g8, pos_b = pos_a + 8;  // positions of this thread's two rows
+  // the last key each of this thread's two rows may see (rows a = g8 and b = g8 + 8)
+  const int pos_a = p.causal ? q0 + wrow + g8 : last_key, pos_b = p.causal ? pos_a + 8 : last_key;
+  const int warp_first = p.causal ? q0 + wrow : last_key;  // the smallest such limit in the warp
   float o[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnP
     }
     const int key0 = kt << kPageLog2;
     // a warp whose rows all precede this tile has nothing to add
-    if (key0 <= q0 + wrow + 15) {
+    if (!p.causal || key0 <= q0 + wrow + 15) {
       const unsigned char* kb = ks + (kt & 1) * kKeys * D * 2;
       const unsigned char* vb = vs + (kt & 1) * kKeys * D * 2;
       // ---- S = Q K^T: 8 n-tiles of 8 keys
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(128, 2) prefill_attn_kernel(const PrefillAttnP
         }
       }
       // ---- scale, causal mask, online softmax (rows a = g8, b = g8 + 8)
-      const bool diag = key0 + kKeys - 1 > q0 + wrow;  // some key follows some row of the warp
+      const bool diag = key0 + kKeys - 1 > warp_first;  // some key lies past some row's limit
       float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {

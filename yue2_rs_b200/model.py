@@ -98,11 +98,14 @@ class Model:
 
     # ---- construction
     @classmethod
-    def open(cls, path, device=0, loader="native"):
+    def open(cls, path, device=0, loader="native", nar=False):
         """Model::open (src/model.rs:418-451): config.json + safetensors under `path`. The
         native loader (yue2_model_load_checkpoint) validates the headers and uploads through
-        pinned staging; loader="python" reads with numpy and calls set_tensor per tensor."""
+        pinned staging; loader="python" reads with numpy and calls set_tensor per tensor.
+        nar=True also loads the flow-matching tensors that `velocity` uses."""
         m = cls(Config.read(os.path.join(path, "config.json")), device)
+        if nar:
+            m.enable_nar()
         if loader == "native":
             _lib.check(_lib.lib().yue2_model_load_checkpoint(m._h, os.fsencode(path), None))
         else:
@@ -113,13 +116,21 @@ class Model:
         return m
 
     @classmethod
-    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, device=0):
+    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, device=0, nar=False):
         """Seeded synthetic weights generated on the device: matrices N(0, std), RMSNorm
-        gains norm_mean + N(0, std), bf16."""
+        gains norm_mean + N(0, std), bf16. nar=True adds the flow-matching tensors."""
         m = cls(config, device)
+        if nar:
+            m.enable_nar()
         _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, seed, std, norm_mean))
         m.finalize()
         return m
+
+    def enable_nar(self):
+        """Device slots for the NAR tensors (yue2_model_enable_nar); load them afterwards."""
+        c = self.config
+        _lib.check(_lib.lib().yue2_model_enable_nar(self._h, c.latent_dim, c.max_latent_frames, c.timestep_shift))
+        return self
 
     def set_tensor(self, name, arr, dtype=None, rows=None, cols=None):
         arr = np.ascontiguousarray(arr)
@@ -193,6 +204,16 @@ class Model:
         _lib.check(_lib.lib().yue2_prefill(self._h, cache._h, _ptr(ids), ids.size, int(Phase.VOCAB),
                                            _ptr(out) if logits else None))
         return cache, out
+
+
+    def velocity(self, state, cache, raw_t):
+        """Model::velocity (model.rs:611-697, nar_cond_end 0): [rows, latent_dim] f32 velocity
+        of the bf16-valued latent frames `state` at logit time `raw_t` over `cache`'s prefix."""
+        state = np.ascontiguousarray(state, dtype=np.float32).reshape(-1, self.config.latent_dim)
+        out = np.empty_like(state)
+        _lib.check(_lib.lib().yue2_velocity(self._h, cache._h, _ptr(state), state.shape[0], float(raw_t),
+                                            _ptr(out)))
+        return out
 
 
 class Cache:
