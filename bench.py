@@ -368,7 +368,10 @@ def main():
     # to the prefix, the codec ids and every frame)
     nar = {}
     if not args.no_sweep:
-        nm = Model.synthetic(cfg, seed=4, std=0.02, norm_mean=1.0, device=local, nar=True)
+        import copy
+        cn = copy.copy(cfg)
+        cn.vocab_size = 184704  # the codec ids synthesize prefills
+        nm = Model.synthetic(cn, seed=4, std=0.02, norm_mean=1.0, device=local, nar=True)
         frames = (24576 - PROMPT - 3) // 2
         length = PROMPT + frames + 1
         nc = nm.new_cache(24576)
@@ -391,12 +394,26 @@ def main():
         lin = 2.0 * n * cfg.num_hidden_layers * H * (qd + 2 * kd + qd + 3 * I)
         att = 4.0 * n * (length + n) * cfg.num_attention_heads * D * cfg.num_hidden_layers
         nc.close()
+        # one song through Model::synthesize: a 1,024-id prefix, 4,096 codec frames (one
+        # chunk), 4 midpoint steps = 8 velocity calls, host ids in / latents out
+        rs = np.random.default_rng(rank + 1)
+        sp = rs.integers(0, 151851, PROMPT).tolist()
+        sc = rs.integers(0, 32768, 4096).tolist()
+        nm.synthesize(sp, sc, seed=1, steps=1)
+        barrier()
+        t0 = time.perf_counter()
+        lat = nm.synthesize(sp, sc, seed=2, steps=4)
+        syn_s = max_over_ranks(time.perf_counter() - t0)
+        assert np.isfinite(lat).all()
         nm.close()
         nar = {"frames": frames, "prefix_positions": length, "ms_per_velocity": vms,
                "frames_per_s": world * frames / (vms / 1000.0), "linear_tflop": lin / 1e12,
                "attention_tflop": att / 1e12, "achieved_tflops": (lin + att) / (vms * 1e-3) / 1e12,
                "what": "yue2_velocity with host state in / velocity out, 3B-shaped NAR layers (synthetic), "
-                       "one call = every frame through 28 layers; synthesize makes 2 per ODE step"}
+                       "one call = every frame through 28 layers; synthesize makes 2 per ODE step",
+               "synthesize": {"prefix": PROMPT, "frames": 4096, "steps": 4, "seconds": syn_s,
+                              "frames_per_s": world * 4096 / syn_s,
+                              "what": "yue2_synthesize: prefill of 5,121 ids + 8 velocity calls of 4,098 rows"}}
 
     # ---- end to end through the public C ABI with host buffers (prefill included)
     barrier()

@@ -214,6 +214,19 @@ int yue2_prefill(Yue2Model* m, Yue2Cache* c, const int64_t* ids, uint64_t n, int
  * or 128. */
 int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uint64_t rows, double raw_t, float* out);
 
+/* Model::synthesize (src/model.rs:699-776): the acoustic latents [codec_len, 64] (host) of
+ * one song. Chunks of (min(24576, max_position_embeddings) - prefix_len - 3) / 2 frames:
+ * each prefills prefix + (codec + CODEC_OFFSET) + MUSIC_END into its own cache, then runs
+ * `steps` midpoint steps (two yue2_velocity calls each) from the chunk's slice of the
+ * song's noise (yue2_noise(seed, codec_len, 64)). Codec ids in [0, 32768); the reference's
+ * errors: "Expected nonempty codec tokens and a 64-dimensional latent model", "Prefix leaves
+ * no acoustic context", "Flow matching produced nonfinite latents". */
+int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, const int64_t* codec,
+                    uint64_t codec_len, uint64_t seed, uint64_t steps, float* out);
+/* Generator::new(seed).normal_tensor(rows, cols) (src/sampling.rs:63-78) on the host:
+ * rows * cols a multiple of 16. Needs no device. */
+int yue2_noise(uint64_t seed, uint64_t rows, uint64_t cols, float* out);
+
 /* Request-local MT19937 (src/sampling.rs:10-62), state kept on the device of `m`. */
 int yue2_rng_create(Yue2Model* m, uint64_t seed, Yue2Rng** out);
 void yue2_rng_free(Yue2Rng* r);

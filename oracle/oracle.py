@@ -60,6 +60,8 @@ _P = {
                              c_p, ctypes.POINTER(c_u64), ctypes.POINTER(c_int)]),
     "orc_model_nar": (c_int, [c_p, c_u64, c_u64, c_f]),
     "orc_velocity": (c_int, [c_p, c_p, c_p, c_u64, ctypes.c_double, c_p]),
+    "orc_normal_tensor": (c_int, [c_u64, c_u64, c_u64, c_p]),
+    "orc_synthesize": (c_int, [c_p, c_p, c_u64, c_p, c_u64, c_u64, c_u64, c_p]),
 }
 
 _lib = None
@@ -181,6 +183,14 @@ class OracleModel:
         _ck(lib().orc_velocity(self._h, cache._h, _ptr(st), st.shape[0], float(raw_t), _ptr(out)))
         return out
 
+    def synthesize(self, prefix, codec, seed, steps):
+        """Model::synthesize (src/model.rs:699-776): latents [len(codec), 64]."""
+        p = np.ascontiguousarray(prefix, dtype=np.int64)
+        c = np.ascontiguousarray(codec, dtype=np.int64)
+        out = np.empty((c.size, 64), dtype=np.float32)
+        _ck(lib().orc_synthesize(self._h, _ptr(p), p.size, _ptr(c), c.size, seed, steps, _ptr(out)))
+        return out
+
     def hidden(self, ids, cache):
         ids = np.ascontiguousarray(ids, dtype=np.int64)
         out = np.empty((ids.size, self.config.hidden_size), dtype=np.float32)
@@ -261,6 +271,13 @@ class OracleRng:
             lib().orc_rng_free(self._h)
         except Exception:
             pass
+
+
+def normal_tensor(seed, rows, cols):
+    """Generator::new(seed).normal_tensor(rows, cols) (src/sampling.rs:63-78)."""
+    out = np.empty((rows, cols), dtype=np.float32)
+    _ck(lib().orc_normal_tensor(seed, rows, cols, _ptr(out)))
+    return out
 
 
 def choose(logits, sampling, history, step, phase, legacy, rng):

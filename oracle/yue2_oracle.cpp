@@ -907,3 +907,76 @@ ORC_API int orc_velocity(void* mp, void* cp, const float* state, uint64_t rows, 
   for (size_t i = 0; i < rows * D; ++i) out[i] = lat[D + i];
   return 0;
 }
+
+// Generator::normal_tensor (src/sampling.rs:63-78): every element first draws uniform_f32;
+// then in each block of 16, elements i and i + 8 (i < 8) become a Box-Muller pair in f32
+// (the angle is formed in f64 and cast).
+static void normal_tensor(uint64_t seed, size_t count, float* out) {
+  Rng g;
+  rng_init(g, seed);
+  for (size_t i = 0; i < count; ++i) out[i] = (float)(rng_next(g) & 0x00ffffffu) / 16777216.0f;
+  for (size_t b = 0; b + 16 <= count; b += 16) {
+    float* blk = out + b;
+    for (int i = 0; i < 8; ++i) {
+      const float radius = sqrtf(-2.f * logf(1.f - blk[i]));
+      const float theta = (float)(2.0 * 3.14159265358979323846 * (double)blk[i + 8]);
+      blk[i] = radius * cosf(theta);
+      blk[i + 8] = radius * sinf(theta);
+    }
+  }
+}
+
+ORC_API int orc_normal_tensor(uint64_t seed, uint64_t rows, uint64_t cols, float* out) {
+  const size_t n = rows * cols;
+  if (n < 16 || n % 16) return fail("normal_tensor needs a multiple of 16 elements");
+  normal_tensor(seed, n, out);
+  return 0;
+}
+
+// logit (src/model.rs:778-780)
+static double logit(double t) { return std::min(20.0, std::max(-20.0, std::log(t / (1.0 - t)))); }
+
+// Model::synthesize (src/model.rs:699-776): chunks of `size` codec frames; each chunk
+// prefills prefix + codec ids + MUSIC_END, then runs `steps` midpoint steps of the flow ODE
+// from the chunk's slice of one song-wide noise tensor. out [codec_len, 64].
+ORC_API int orc_synthesize(void* mp, const int64_t* prefix, uint64_t plen, const int64_t* codec, uint64_t clen,
+                           uint64_t seed, uint64_t steps, float* out) {
+  Model& m = *(Model*)mp;
+  const uint64_t kContext = 24576, kMusicEnd = 151852, kCodecOffset = 151853, kCodecSize = 32768;
+  if (!m.nar_on || m.latent != 64 || clen == 0 || steps == 0)
+    return fail("Expected nonempty codec tokens and a 64-dimensional latent model");
+  for (uint64_t i = 0; i < clen; ++i)
+    if (codec[i] < 0 || (uint64_t)codec[i] >= kCodecSize)
+      return fail("Expected nonempty codec tokens and a 64-dimensional latent model");
+  const uint64_t capacity = std::min<uint64_t>(kContext, m.c.max_pos);
+  if (capacity < plen + 3 || (capacity - (plen + 3)) / 2 == 0) return fail("Prefix leaves no acoustic context");
+  const uint64_t size = (capacity - (plen + 3)) / 2;
+  const size_t D = 64;
+  std::vector<float> noise(clen * D);
+  normal_tensor(seed, noise.size(), noise.data());
+  const float dt = 1.f / (float)steps;
+  for (uint64_t start = 0; start < clen; start += size) {
+    const uint64_t end = std::min(start + size, clen), rows = end - start;
+    std::vector<int64_t> ids(prefix, prefix + plen);
+    for (uint64_t i = start; i < end; ++i) ids.push_back(codec[i] + (int64_t)kCodecOffset);
+    ids.push_back((int64_t)kMusicEnd);
+    Cache* cache = (Cache*)orc_cache_create(mp, ids.size());
+    int rc = orc_prefill(mp, cache, ids.data(), ids.size(), 2, nullptr);
+    std::vector<float> state(noise.begin() + start * D, noise.begin() + end * D), first(rows * D), mid(rows * D),
+        vel(rows * D);
+    for (auto& v : state) v = round_bf16(v);
+    for (uint64_t step = 0; step < steps && !rc; ++step) {
+      const double t = 1.0 - (double)step / (double)steps;
+      if ((rc = orc_velocity(mp, cache, state.data(), rows, logit(t), first.data()))) break;
+      for (size_t i = 0; i < state.size(); ++i) mid[i] = round_bf16(state[i] - round_bf16(first[i] * (dt / 2.f)));
+      if ((rc = orc_velocity(mp, cache, mid.data(), rows, logit(t - 0.5 / (double)steps), vel.data()))) break;
+      for (size_t i = 0; i < state.size(); ++i) state[i] = round_bf16(state[i] - round_bf16(vel[i] * dt));
+    }
+    delete cache;
+    if (rc) return rc;
+    for (float v : state)
+      if (!std::isfinite(v)) return fail("Flow matching produced nonfinite latents");
+    memcpy(out + start * D, state.data(), state.size() * 4);
+  }
+  return 0;
+}

@@ -72,3 +72,11 @@ def c1_prompt(c1_config):
     """256 token ids uniform over the vocabulary (seeded) and 64 teacher-forced ids."""
     rng = np.random.default_rng(12345)
     return (rng.integers(0, c1_config.vocab_size, 256).tolist(), rng.integers(0, c1_config.vocab_size, 64).tolist())
+
+
+@pytest.fixture(scope="session")
+def nar_tiny_dir(tmp_path_factory):
+    """The small real-vocabulary model (unit-mean gains) with its NAR tensors."""
+    from yue2_rs_b200 import synth
+    return synth.write_checkpoint(str(tmp_path_factory.mktemp("nar_tiny")), synth.config_nar_tiny(), seed=6,
+                                  norm_mean=1.0)

@@ -103,6 +103,8 @@ _PROTOS = {
     "yue2_forward": (c_int, [c_p, c_p, c_p, c_u64, c_int, c_p]),
     "yue2_prefill": (c_int, [c_p, c_p, c_p, c_u64, c_int, c_p]),
     "yue2_velocity": (c_int, [c_p, c_p, c_p, c_u64, ctypes.c_double, c_p]),
+    "yue2_synthesize": (c_int, [c_p, c_p, c_u64, c_p, c_u64, c_u64, c_u64, c_p]),
+    "yue2_noise": (c_int, [c_u64, c_u64, c_u64, c_p]),
     "yue2_rng_create": (c_int, [c_p, c_u64, ctypes.POINTER(c_p)]),
     "yue2_rng_free": (None, [c_p]),
     "yue2_rng_state": (c_int, [c_p, c_p, ctypes.POINTER(c_u64)]),

@@ -216,6 +216,22 @@ class Model:
         return out
 
 
+    def synthesize(self, prefix, codec, seed, steps=32):
+        """Model::synthesize (model.rs:699-776): latents [len(codec), 64] of one song."""
+        p = np.ascontiguousarray(prefix, dtype=np.int64)
+        c = np.ascontiguousarray(codec, dtype=np.int64)
+        out = np.empty((c.size, 64), dtype=np.float32)
+        _lib.check(_lib.lib().yue2_synthesize(self._h, _ptr(p), p.size, _ptr(c), c.size, seed, steps, _ptr(out)))
+        return out
+
+
+def noise(seed, rows, cols):
+    """Generator::new(seed).normal_tensor(rows, cols) (sampling.rs:63-78), on the host."""
+    out = np.empty((rows, cols), dtype=np.float32)
+    _lib.check(_lib.lib().yue2_noise(seed, rows, cols, _ptr(out)))
+    return out
+
+
 class Cache:
     """Cache (src/model.rs:276-306): paged bf16 KV on the device, released on drop."""
 

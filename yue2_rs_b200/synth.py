@@ -94,6 +94,15 @@ def config_c1():
                   max_position_embeddings=24576, max_latent_frames=16)
 
 
+def config_nar_tiny():
+    """A small model with the real 184,704-id vocabulary (the codec ids of the acoustic
+    stage) and a 160-position context, so that a song of a few hundred frames spans several
+    synthesize chunks: 2 layers, hidden 256, 4/2 heads of 64, intermediate 512."""
+    return Config(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                  intermediate_size=512, vocab_size=184704, rms_norm_eps=1e-6, rope_theta=10000.0,
+                  max_position_embeddings=160, max_latent_frames=16)
+
+
 def config_c2():
     """3B-shaped AR model: 28 layers, hidden 3072, 24/8 heads, intermediate 8192."""
     return Config(hidden_size=3072, num_hidden_layers=28, num_attention_heads=24, num_key_value_heads=8,
