@@ -184,6 +184,9 @@ def main():
     ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
                     help="one N-id prefill of the config-1 model and exit: the command line for the "
                          "prefill's ncu launch list")
+    ap.add_argument("--velocity-profile", type=int, default=0, metavar="F",
+                    help="one Model::velocity call of F latent frames after a synthetic 1,025-position "
+                         "prefix (3B-shaped NAR model; --profile-layers N for a smaller one) and exit")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -205,8 +208,25 @@ def main():
         return dp.max(x)
 
     cfg = synth.config_c2()
-    if args.profile and args.profile_layers > 0:
+    if (args.profile or args.velocity_profile) and args.profile_layers > 0:
         cfg.num_hidden_layers = args.profile_layers
+    if args.velocity_profile:
+        nm = Model.synthetic(cfg, seed=4, std=0.02, norm_mean=1.0, device=local, nar=True)
+        frames = args.velocity_profile
+        nc = nm.new_cache(PROMPT + 1 + frames + 2)
+        nc.fill_normal(PROMPT + 1, seed=5)
+        st = np.random.default_rng(0).standard_normal((frames, cfg.latent_dim)).astype(np.float32)
+        nm.velocity(st, nc, 0.5)  # first call per shape: cuBLASLt candidate timing
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        v = nm.velocity(st, nc, 0.5)
+        ms = (time.perf_counter() - t0) * 1000.0
+        print(json.dumps({"velocity_profile": True, "frames": frames, "layers": cfg.num_hidden_layers,
+                          "ms": ms, "finite": bool(np.isfinite(v).all())}), flush=True)
+        nc.close()
+        nm.close()
+        dp.close()
+        return 0
     model = Model.synthetic(cfg, seed=1, std=0.02, device=local)
     if args.prefill_profile:
         ids = np.random.default_rng(5).integers(0, cfg.vocab_size, args.prefill_profile).tolist()

@@ -409,7 +409,12 @@ static int encode_layers(Yue2Model& m, PrefillBufs& P, const std::vector<LayerW>
         fp.pos0 = pos0;
         fp.scale = 1.0f / sqrtf((float)g.dim);
         fp.causal = causal ? 1 : 0;
-        CK(launch_prefill_attention(s, fp));
+        fp.error = m.flags + 2;
+        if (m.prefill_attn_tc5 && prefill_attention_tc_supported(g)) {
+          CK(launch_prefill_attention_tc(s, fp));
+        } else {
+          CK(launch_prefill_attention(s, fp));
+        }
       } else if ((rc = row_attention(m, P, rows, l, R, splits, false))) {
         return rc;
       }

@@ -101,6 +101,7 @@ struct PrefillAttnParams {
   int layer, C, pos0;
   float scale;
   int causal;  // 1: row r sees keys up to pos0 + r; 0: every row sees keys up to pos0 + C - 1
+  int32_t* error;  // set when a bounded wait of the tcgen05 form gave up
 };
 
 struct RopeParams {
@@ -205,6 +206,9 @@ cudaError_t launch_gemm_tc(cudaStream_t s, const uint16_t* W, int N, int K, cons
 cudaError_t launch_gemm_tc_swiglu(cudaStream_t s, const uint16_t* Wgu, int I, int K, const uint16_t* X, int ldx,
                                   uint16_t* H, int ldh, int C, int32_t* error);
 cudaError_t launch_prefill_attention(cudaStream_t s, const PrefillAttnParams& p);
+// The same attention on tcgen05 (kernels_prefill_attn_tc.cu): head_dim 128.
+bool prefill_attention_tc_supported(const Geometry& g);
+cudaError_t launch_prefill_attention_tc(cudaStream_t s, const PrefillAttnParams& p);
 cudaError_t launch_step_end(cudaStream_t s, bool pdl, DevRow* rows, int R);
 cudaError_t launch_mt_words(cudaStream_t s, MtState* st, uint32_t* words, int nwords, const SampleReq* reqs,
                             int nreq);

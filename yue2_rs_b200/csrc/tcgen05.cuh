@@ -1,0 +1,101 @@
+// Inline-PTX wrappers for the 5th-generation tensor cores (sm_100a) shared by the tcgen05
+// kernels: mbarriers with bounded waits, 128-byte-swizzled K-major shared-memory matrix
+// descriptors, kind::f16 MMAs into TMEM, commits, TMEM loads and the proxy fences.
+#pragma once
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace y2 {
+namespace tc {
+
+Y2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+Y2_DEV void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+Y2_DEV void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+Y2_DEV bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of the given parity, at most `spins` polls; false (and *error set)
+// when it gave up.
+Y2_DEV bool mbar_wait_bounded(uint64_t* b, uint32_t parity, int32_t* error, long spins) {
+  for (long i = 0; i < spins; ++i)
+    if (mbar_try_wait(b, parity)) return true;
+  atomicExch(error, 1);
+  return false;
+}
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of
+// 128 B, 8-row groups 1024 B apart (stride byte offset), descriptor version 1. The tile
+// starts on a 1024-byte boundary; a K step of 16 bf16 within the 128-byte row adds 32 B to
+// the start address.
+Y2_DEV uint64_t sdesc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1 << 46;            // version
+  d |= (uint64_t)2 << 61;            // layout: 128-byte swizzle
+  return d;
+}
+// Byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled K-major tile.
+__host__ __device__ constexpr uint32_t sw128(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Instruction descriptor of kind::f16: dense, D f32, A and B bf16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, issued by one thread.
+Y2_DEV void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The mbarrier receives one arrival when every MMA this thread issued before has finished.
+Y2_DEV void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+Y2_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+Y2_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Generic-proxy writes to shared memory (st.shared, cp.async, stmatrix) made visible to the
+// tensor cores' (async proxy) reads.
+Y2_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes 32 (w % 4) ..).
+Y2_DEV void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Four 8x8 b16 matrices to shared memory from this lane's fragments (the ldmatrix layout):
+// lane i gives the address of row i % 8 of matrix i / 8.
+Y2_DEV void stsm_x4(void* smem, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(smem_u32(smem)), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+}  // namespace tc
+}  // namespace y2
