@@ -1,5 +1,6 @@
-"""The tcgen05 chunk attention (YUE2_CUDA_PREFILL_ATTN=tc, head_dim 128) against the
-oracle and against the mma.sync chunk attention, on the unit-gain reduced model:
+"""The tcgen05 chunk attention (the default for head_dim 128) against the oracle and
+against the mma.sync chunk attention (YUE2_CUDA_PREFILL_ATTN=sync), on the unit-gain
+reduced model:
 
   * causal: a GEMM prefill in chunks of 300 positions (later chunks attend to earlier
     chunks' K/V, partial row tiles) within the prefill tolerance of the oracle;
@@ -47,7 +48,7 @@ def tc5(c1u_dir):
 
 @pytest.fixture(scope="module")
 def sync(c1u_dir):
-    m = _open(c1u_dir, YUE2_CUDA_PREFILL_CHUNK=300)
+    m = _open(c1u_dir, YUE2_CUDA_PREFILL_ATTN="sync", YUE2_CUDA_PREFILL_CHUNK=300)
     yield m
     m.close()
 

@@ -279,7 +279,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
     m->prefill_chunk = std::max(16, std::min(kPrefillRows, env_int("YUE2_CUDA_PREFILL_CHUNK", kPrefillRows)));
     const char* a = getenv("YUE2_CUDA_PREFILL_ATTN");
     m->prefill_tc_attn = !(a && std::string(a) == "rows");
-    m->prefill_attn_tc5 = a && std::string(a) == "tc";
+    m->prefill_attn_tc5 = !a ? 0 : std::string(a) == "tc" ? 1 : std::string(a) == "sync" ? 2 : 0;
     m->gemm_split_k = env_int("YUE2_CUDA_GEMM_SPLITK", 0) != 0;
     m->wide_min = std::max(2, std::min(kMaxRows + 1, env_int("YUE2_CUDA_WIDE_MIN", 3)));
     const char* gm = getenv("YUE2_CUDA_GEMM");

@@ -56,7 +56,9 @@ struct Yue2Model {
   bool use_prefill_gemm = true;  // prompts of >= kPrefillGemmMin ids as GEMMs (YUE2_CUDA_PREFILL=gemv: off)
   int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
   bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
-  bool prefill_attn_tc5 = false;  // its tcgen05 form for head_dim 128 (YUE2_CUDA_PREFILL_ATTN=tc)
+  // its tcgen05 form for head_dim 128: 0 when the grid fills two waves of the SMs (else the
+  // mma.sync form), 1 always (YUE2_CUDA_PREFILL_ATTN=tc), 2 never (=sync)
+  int prefill_attn_tc5 = 0;
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
   bool gemm_tc = false;          // GEMMs of >= 128 rows on the tcgen05 kernel (YUE2_CUDA_GEMM=tc), else cuBLASLt

@@ -410,7 +410,8 @@ static int encode_layers(Yue2Model& m, PrefillBufs& P, const std::vector<LayerW>
         fp.scale = 1.0f / sqrtf((float)g.dim);
         fp.causal = causal ? 1 : 0;
         fp.error = m.flags + 2;
-        if (m.prefill_attn_tc5 && prefill_attention_tc_supported(g)) {
+        const bool wide = (long)((R + 127) / 128) * g.heads >= 2L * m.sms;  // tcgen05 tiles: 128 rows
+        if (prefill_attention_tc_supported(g) && (m.prefill_attn_tc5 == 1 || (m.prefill_attn_tc5 == 0 && wide))) {
           CK(launch_prefill_attention_tc(s, fp));
         } else {
           CK(launch_prefill_attention(s, fp));

@@ -15,8 +15,9 @@
 //   4. one thread issues O_t = P_hi.V + P_lo.V (M 128, N 128, K 64: 8 MMAs) into TMEM
 //      columns 128..255; each thread adds its row of O_t into its f32 accumulator in
 //      registers after scaling that by exp(m_old - m_new).
-// The steps run one after another within a CTA; two CTAs per SM overlap one's softmax with
-// the other's MMAs and copies. Every wait on an MMA is bounded: when one gives up, the CTA
+// The next page's K copies start as soon as S is computed and its V copies as soon as O_t
+// is, so they run under the softmax and the accumulation; two CTAs per SM overlap one's
+// softmax with the other's MMAs. Every wait on an MMA is bounded: when one gives up, the CTA
 // sets the model's error flag, stops, and still frees its TMEM.
 #include <cuda_runtime.h>
 
@@ -106,20 +107,34 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
   uint32_t phase = 0;
   bool ok = true;
 
-  for (int kt = 0; kt < nkt && ok; ++kt) {
-    // ---- 1. K tile (swizzled, K-major) and V staging ([key][256 B], chunk c at c ^ (key & 7))
+  // copies of one page: K into its swizzled K-major tile, V into the staging tile
+  // ([key][256 B], chunk c at c ^ (key & 7)); keys past last_key are zero-filled
+  auto load_k = [&](int kt) {
     const uint16_t* page = reinterpret_cast<const uint16_t*>(p.pages[kt]);
     for (int i = tid; i < KT * 16; i += THREADS) {
       const int r = i >> 4, c = i & 15;
       const bool valid = (kt << kPageLog2) + r <= last_key;
-      const size_t off = (size_t)(valid ? r : 0) * D + c * 8;
-      cp_async16_zfill(ks + (c >> 3) * (KT * 128) + tc::sw128(r, c & 7), page + koff + off, valid);
-      cp_async16_zfill(vstage + r * 256 + ((c ^ (r & 7)) << 4), page + voff + off, valid);
+      cp_async16_zfill(ks + (c >> 3) * (KT * 128) + tc::sw128(r, c & 7),
+                       page + koff + (size_t)(valid ? r : 0) * D + c * 8, valid);
     }
     cp_async_commit();
+  };
+  auto load_v = [&](int kt) {
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(p.pages[kt]);
+    for (int i = tid; i < KT * 16; i += THREADS) {
+      const int r = i >> 4, c = i & 15;
+      const bool valid = (kt << kPageLog2) + r <= last_key;
+      cp_async16_zfill(vstage + r * 256 + ((c ^ (r & 7)) << 4), page + voff + (size_t)(valid ? r : 0) * D + c * 8,
+                       valid);
+    }
+    cp_async_commit();
+  };
+  // waits for the copies, then V^T: 8 key blocks x 16 dim blocks of 8 x 8, each warp moving
+  // 4 x 8 of them (ldmatrix.trans, stmatrix); ends with the tile ready for the tensor cores
+  auto stage_v = [&]() {
     cp_async_wait<0>();
+    tc::fence_before();
     __syncthreads();
-    // V^T: 8 key blocks x 16 dim blocks of 8 x 8; each warp moves 4 x 8 of them
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int j = warp * 8 + u;          // 0..31
@@ -129,13 +144,18 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
       uint32_t f[4];
       const int key = kb * 8 + rr;
       ldsm_x4_trans(f, vstage + key * 256 + ((db ^ (key & 7)) << 4));
-      const int dim = db * 8 + rr;
-      tc::stsm_x4(vt + tc::sw128(dim, kb), f);
+      tc::stsm_x4(vt + tc::sw128(db * 8 + rr, kb), f);
     }
     tc::fence_proxy_async();
     tc::fence_before();
     __syncthreads();
+  };
 
+  load_k(0);
+  load_v(0);
+  stage_v();
+  for (int kt = 0; kt < nkt && ok; ++kt) {
+    const bool more = kt + 1 < nkt;
     // ---- 2. S = Q . K^T
     if (tid == 0) {
       tc::fence_after();
@@ -152,6 +172,7 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc::fence_after();
+    if (more) load_k(kt + 1);  // the K tile is free: the next page's keys load under the softmax
 
     // ---- 3. softmax of this thread's row; P = hi + lo into shared memory
     float s[KT];
@@ -214,6 +235,7 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc::fence_after();
+    if (more) load_v(kt + 1);  // P and V^T are free: the next page's values load under the sums
 #pragma unroll
     for (int c = 0; c < D / 32; ++c) {
       uint32_t v[32];
@@ -221,9 +243,10 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
 #pragma unroll
       for (int j = 0; j < 32; ++j) o[32 * c + j] = o[32 * c + j] * alpha + __uint_as_float(v[j]);
     }
-    tc::fence_before();
-    __syncthreads();  // the next tile overwrites K, V^T, P and both TMEM regions
+    if (more) stage_v();  // also orders this tile's TMEM reads before the next tile's MMAs
   }
+  if (!ok) cp_async_wait<0>();
+
 
   // ---- normalise and store bf16 (rows of this chunk only)
   if (ok && tid < nrows) {
