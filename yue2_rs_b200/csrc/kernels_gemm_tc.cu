@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace y2 {
 namespace {
@@ -47,31 +48,17 @@ struct TcGemmArgs {
   int32_t* error;
 };
 
-Y2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-Y2_DEV void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
+using tc::mbar_init;
+using tc::mbar_try_wait;
+using tc::sdesc_sw128;
+using tc::smem_u32;
+using tc::tmem_ld32;
 Y2_DEV void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
 }
-Y2_DEV bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 // Bounded wait for the phase of the given parity; false (and *error set) when it gave up.
 Y2_DEV bool mbar_wait(uint64_t* b, uint32_t parity, int32_t* error) {
-  for (long i = 0; i < kSpin; ++i)
-    if (mbar_try_wait(b, parity)) return true;
-  atomicExch(error, 1);
-  return false;
+  return tc::mbar_wait_bounded(b, parity, error, kSpin);
 }
 
 Y2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
@@ -82,51 +69,19 @@ Y2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
       : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of
-// 128 B, 8-row groups 1024 B apart (stride byte offset), descriptor version 1.
-Y2_DEV uint64_t sdesc_sw128(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1 << 16;              // leading byte offset (unused by swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
-  d |= (uint64_t)1 << 46;              // version
-  d |= (uint64_t)2 << 61;              // layout: 128-byte swizzle
-  return d;
-}
-
 // Instruction descriptor: dense, D f32, A and B bf16, both K-major, N = BN, M = BM.
 template <int BN>
 __host__ __device__ constexpr uint32_t idesc() {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  return tc::idesc_bf16(BM, BN);
 }
 
 template <int BN>
 Y2_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc<BN>()), "r"(accumulate)
-      : "memory");
+  tc::mma_bf16(tmem_d, adesc, bdesc, idesc<BN>(), accumulate);
 }
-Y2_DEV void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-Y2_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-Y2_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive f32 columns of this thread's TMEM lane.
-Y2_DEV void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+Y2_DEV void umma_commit(uint64_t* bar) { tc::commit(bar); }
+Y2_DEV void tc_fence_before() { tc::fence_before(); }
+Y2_DEV void tc_fence_after() { tc::fence_after(); }
 
 // 32 bf16 outputs (packed in pairs) of one row: four 16-byte stores, or element stores at
 // the ragged right edge of the matrix.

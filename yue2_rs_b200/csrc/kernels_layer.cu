@@ -389,17 +389,23 @@ cudaError_t launch_gemv(cudaStream_t s, bool pdl, int xmode, int epi, const Gemv
 }
 
 // ------------------------------------------------------------------ QK norm + RoPE + KV append
-// One warp per (head, row): q heads are normalised (Norm::heads) and rotated, k heads
-// normalised, rotated and written to the row's page at its position, v heads copied.
+// One warp per (head, row), kRopeWarps heads of one row per CTA: q heads are normalised
+// (Norm::heads) and rotated, k heads normalised, rotated and written to the row's page at
+// its position, v heads copied. Each lane stores D / 32 consecutive elements.
+constexpr int kRopeWarps = 8;
+
 template <int D>
-__global__ void __launch_bounds__(32) rope_append_kernel(const RopeParams p) {
+__global__ void __launch_bounds__(32 * kRopeWarps) rope_append_kernel(const RopeParams p) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float v[D];
-  const int hix = blockIdx.x, r = blockIdx.y, lane = threadIdx.x;
+  constexpr int DL = D / 32;  // elements per lane: 2, 4 or 8
+  __shared__ float vbuf[kRopeWarps][D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hix = blockIdx.x * kRopeWarps + warp, r = blockIdx.y;
+  const Geometry& g = p.g;
+  if (hix >= g.heads + 2 * g.kvh) return;
   const DevRow row = p.rows[r];
   if (!row.active) return;
-  const Geometry& g = p.g;
   const int pos = row.pos;
   if (pos < 0 || pos >= p.max_pos) {
     if (lane == 0) atomicExch(p.error, 1);
@@ -412,25 +418,33 @@ __global__ void __launch_bounds__(32) rope_append_kernel(const RopeParams p) {
   if (hix >= g.heads + g.kvh) {  // value head: already bf16 (Linear::finish)
     const int head = hix - g.heads - g.kvh;
     uint16_t* dst = page + kv_offset(g, p.layer, 1, head) + (size_t)slot * D;
-    for (int i = lane; i < D; i += 32) dst[i] = src[i];
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + lane * DL);
+    uint32_t* d32 = reinterpret_cast<uint32_t*>(dst + lane * DL);
+#pragma unroll
+    for (int e = 0; e < DL / 2; ++e) d32[e] = __ldcg(s32 + e);
     return;
   }
+  float* v = vbuf[warp];
   const bool is_q = hix < g.heads;
   norm_rope_head<D>(src, is_q ? p.q_norm : p.k_norm, g.eps, p.cos_tab + (size_t)pos * (D / 2),
                     p.sin_tab + (size_t)pos * (D / 2), v);
   uint16_t* dst = is_q ? p.q_out + (size_t)r * g.heads * D + (size_t)hix * D
                        : page + kv_offset(g, p.layer, 0, hix - g.heads) + (size_t)slot * D;
-  for (int i = lane; i < D; i += 32) dst[i] = f2bf_exact(v[i]);
+  uint32_t* d32 = reinterpret_cast<uint32_t*>(dst + lane * DL);
+#pragma unroll
+  for (int e = 0; e < DL / 2; ++e)
+    d32[e] = (uint32_t)f2bf_exact(v[lane * DL + 2 * e]) | ((uint32_t)f2bf_exact(v[lane * DL + 2 * e + 1]) << 16);
 }
 
 cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, int R) {
   RopeParams copy = p;
   void* args[] = {&copy};
-  dim3 grid(p.g.heads + 2 * p.g.kvh, R);
+  dim3 grid((p.g.heads + 2 * p.g.kvh + kRopeWarps - 1) / kRopeWarps, R);
+  const dim3 block(32 * kRopeWarps);
   switch (p.g.dim) {
-    case 64: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<64>, args);
-    case 128: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<128>, args);
-    case 256: return launch_with(s, pdl, grid, dim3(32), 0, (const void*)rope_append_kernel<256>, args);
+    case 64: return launch_with(s, pdl, grid, block, 0, (const void*)rope_append_kernel<64>, args);
+    case 128: return launch_with(s, pdl, grid, block, 0, (const void*)rope_append_kernel<128>, args);
+    case 256: return launch_with(s, pdl, grid, block, 0, (const void*)rope_append_kernel<256>, args);
   }
   return cudaErrorInvalidValue;
 }
