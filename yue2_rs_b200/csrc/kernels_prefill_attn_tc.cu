@@ -6,18 +6,19 @@
 // One CTA of 4 warps takes 128 query rows of one head; thread t owns row t, which is TMEM
 // lane t. Per 64-key tile (one cache page):
 //   1. all threads copy the page's K rows into a 128-byte-swizzled K-major tile and its V
-//      rows into a staging tile (cp.async); the warps transpose V into V^T (dims as rows,
+//      rows into a staging tile; the warps transpose V into V^T (dims as rows,
 //      keys along the row: the K-major B operand of P.V) with ldmatrix.trans + stmatrix;
 //   2. one thread issues S = Q.K^T (M 128, N 64, K 128: 8 MMAs) into TMEM columns 0..63;
 //   3. each thread reads its row of S, masks, updates the running max, and writes its
 //      probabilities as bf16 hi + lo parts (hi + lo carries the f32 value to 2^-16) into two
 //      128-byte-swizzled tiles;
-//   4. one thread issues O_t = P_hi.V + P_lo.V (M 128, N 128, K 64: 8 MMAs) into TMEM
-//      columns 128..255; each thread adds its row of O_t into its f32 accumulator in
-//      registers after scaling that by exp(m_old - m_new).
-// The next page's K copies start as soon as S is computed and its V copies as soon as O_t
-// is, so they run under the softmax and the accumulation; two CTAs per SM overlap one's
-// softmax with the other's MMAs. Every wait on an MMA is bounded: when one gives up, the CTA
+//   4. one thread issues O += P_hi.V + P_lo.V (M 128, N 128, K 64: 8 MMAs); O stays in
+//      TMEM columns 128..255 across pages. Before that, a warp whose rows' running max moved
+//      scales its rows of O by exp(m_old - m_new) (tcgen05.ld, multiply, tcgen05.st), so
+//      O_t = alpha O_(t-1) + P_t V_t as before; the final O is read once.
+// The next page's K copies (cp.async) and V loads (into registers) start as soon as S is
+// computed, so they run under the softmax and P.V; two CTAs per SM overlap one's softmax
+// with the other's MMAs. Every wait on an MMA is bounded: when one gives up, the CTA
 // sets the model's error flag, stops, and still frees its TMEM.
 #include <cuda_runtime.h>
 
@@ -32,7 +33,7 @@ constexpr int D = 128;     // head dim
 constexpr int QROWS = 128; // query rows per CTA (TMEM lanes)
 constexpr int KT = 64;     // keys per tile: one page
 constexpr int THREADS = 128;
-constexpr int TMEM_COLS = 256;  // S: columns 0..63; O_t: columns 128..255
+constexpr int TMEM_COLS = 256;  // S: columns 0..63; O: columns 128..255
 constexpr int O_COL = 128;
 constexpr long kSpin = 1L << 22;
 
@@ -100,9 +101,6 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
   const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
   constexpr uint32_t ID_S = tc::idesc_bf16(QROWS, KT), ID_O = tc::idesc_bf16(QROWS, D);
 
-  float o[D];
-#pragma unroll
-  for (int d = 0; d < D; ++d) o[d] = 0.f;
   float m = -INFINITY, l = 0.f;
   uint32_t phase = 0;
   bool ok = true;
@@ -119,18 +117,29 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
     }
     cp_async_commit();
   };
-  auto load_v = [&](int kt) {
+  // the next page's V: each thread holds 8 chunks of 16 B in registers while the softmax and
+  // P.V of this page run, then writes them to the staging tile ([key][256 B], chunk c at
+  // c ^ (key & 7)) once P.V has released it
+  uint4 vreg[8];
+  auto fetch_v = [&](int kt) {
     const uint16_t* page = reinterpret_cast<const uint16_t*>(p.pages[kt]);
-    for (int i = tid; i < KT * 16; i += THREADS) {
-      const int r = i >> 4, c = i & 15;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = tid + u * THREADS, r = i >> 4, c = i & 15;
       const bool valid = (kt << kPageLog2) + r <= last_key;
-      cp_async16_zfill(vstage + r * 256 + ((c ^ (r & 7)) << 4), page + voff + (size_t)(valid ? r : 0) * D + c * 8,
-                       valid);
+      vreg[u] = valid ? ldg16(page + voff + (size_t)r * D + c * 8) : make_uint4(0u, 0u, 0u, 0u);
     }
-    cp_async_commit();
   };
-  // waits for the copies, then V^T: 8 key blocks x 16 dim blocks of 8 x 8, each warp moving
-  // 4 x 8 of them (ldmatrix.trans, stmatrix); ends with the tile ready for the tensor cores
+  auto put_v = [&]() {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = tid + u * THREADS, r = i >> 4, c = i & 15;
+      *reinterpret_cast<uint4*>(vstage + r * 256 + ((c ^ (r & 7)) << 4)) = vreg[u];
+    }
+  };
+  // waits for the K copies, then V^T from the staging tile: 8 key blocks x 16 dim blocks of
+  // 8 x 8, each warp moving 4 x 8 of them (ldmatrix.trans, stmatrix); ends with both tiles
+  // ready for the tensor cores
   auto stage_v = [&]() {
     cp_async_wait<0>();
     tc::fence_before();
@@ -152,7 +161,8 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
   };
 
   load_k(0);
-  load_v(0);
+  fetch_v(0);
+  put_v();
   stage_v();
   for (int kt = 0; kt < nkt && ok; ++kt) {
     const bool more = kt + 1 < nkt;
@@ -172,7 +182,10 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc::fence_after();
-    if (more) load_k(kt + 1);  // the K tile is free: the next page's keys load under the softmax
+    if (more) {  // the K tile is free: the next page's K and V load under the softmax and P.V
+      load_k(kt + 1);
+      fetch_v(kt + 1);
+    }
 
     // ---- 3. softmax of this thread's row; P = hi + lo into shared memory
     float s[KT];
@@ -211,17 +224,29 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
       *reinterpret_cast<uint4*>(pl + tc::sw128(tid, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     l = l * alpha + sum;
+    // O (in TMEM since the last page) times exp(m_old - m_new), by the warps holding a row
+    // whose max moved; page 0's P.V overwrites O instead
+    if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tc::tmem_ld32(lane_base + O_COL + 32 * c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+        tc::tmem_st32(lane_base + O_COL + 32 * c, v);
+      }
+    }
     tc::fence_proxy_async();
     tc::fence_before();
     __syncthreads();
 
-    // ---- 4. O_t = P_hi . V + P_lo . V
+    // ---- 4. O += P_hi . V + P_lo . V
     if (tid == 0) {
       tc::fence_after();
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
         const uint64_t b = tc::sdesc_sw128(tc::smem_u32(vt + kk * 32));
-        tc::mma_bf16(tmem + O_COL, tc::sdesc_sw128(tc::smem_u32(ph + kk * 32)), b, ID_O, kk > 0);
+        tc::mma_bf16(tmem + O_COL, tc::sdesc_sw128(tc::smem_u32(ph + kk * 32)), b, ID_O, kt > 0 || kk > 0);
       }
 #pragma unroll
       for (int kk = 0; kk < KT / 16; ++kk) {
@@ -235,31 +260,33 @@ __global__ void __launch_bounds__(THREADS, 2) prefill_attn_tc_kernel(const Prefi
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc::fence_after();
-    if (more) load_v(kt + 1);  // P and V^T are free: the next page's values load under the sums
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t v[32];
-      tc::tmem_ld32(lane_base + O_COL + 32 * c, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[32 * c + j] = o[32 * c + j] * alpha + __uint_as_float(v[j]);
+    if (more) {
+      put_v();    // P_lo (the staging tile) and V^T are free
+      stage_v();  // also orders this page's TMEM accesses before the next page's MMAs
     }
-    if (more) stage_v();  // also orders this tile's TMEM reads before the next tile's MMAs
   }
   if (!ok) cp_async_wait<0>();
 
 
-  // ---- normalise and store bf16 (rows of this chunk only)
-  if (ok && tid < nrows) {
+  // ---- normalise and store bf16 (rows of this chunk only); the TMEM loads are warp-wide
+  if (ok) {
     const float inv = 1.0f / l;
     uint16_t* dst = p.out + (size_t)(row0 + tid) * qd + (size_t)h * D;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      uint4 w;
-      w.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-      w.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-      w.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-      w.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-      *reinterpret_cast<uint4*>(dst + 8 * c) = w;
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t v[32];
+      tc::tmem_ld32(lane_base + O_COL + 32 * c, v);
+      if (tid < nrows) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(v[8 * q + 0]) * inv, __uint_as_float(v[8 * q + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(v[8 * q + 2]) * inv, __uint_as_float(v[8 * q + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(v[8 * q + 4]) * inv, __uint_as_float(v[8 * q + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(v[8 * q + 6]) * inv, __uint_as_float(v[8 * q + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + 32 * c + 8 * q) = w;
+        }
+      }
     }
   }
   // after a wait that gave up, the MMAs it waited for get one more bounded wait before
