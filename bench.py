@@ -65,6 +65,15 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def measured_bf16_tflops():
+    """The burst cuBLAS bf16 GEMM peak (TFLOP/s) for a kernel timed alone, and its source."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class Clocks:
     """nvidia-smi samples (200 ms) of this rank's GPU during the timed region."""
 
@@ -426,9 +435,12 @@ def main():
         syn_s = max_over_ranks(time.perf_counter() - t0)
         assert np.isfinite(lat).all()
         nm.close()
+        tf_peak, tf_kind = measured_bf16_tflops()
         nar = {"frames": frames, "prefix_positions": length, "ms_per_velocity": vms,
                "frames_per_s": world * frames / (vms / 1000.0), "linear_tflop": lin / 1e12,
                "attention_tflop": att / 1e12, "achieved_tflops": (lin + att) / (vms * 1e-3) / 1e12,
+               "roofline": {"bound": "tensor", "peak": tf_peak, "unit": "TFLOP/s", "peak_kind": tf_kind,
+                            "frac": (lin + att) / (vms * 1e-3) / 1e12 / tf_peak},
                "what": "yue2_velocity with host state in / velocity out, 3B-shaped NAR layers (synthetic), "
                        "one call = every frame through 28 layers; synthesize makes 2 per ODE step",
                "synthesize": {"prefix": PROMPT, "frames": 4096, "steps": 4, "seconds": syn_s,
