@@ -154,6 +154,59 @@ def cpu_baseline(config, steps_budget_s=20.0, threads=None):
                       f"of the reference decode math, not Accelerate"}
 
 
+def velocity_flops(config, n, keys):
+    """FLOPs of one Model::velocity call over n rows (latent frames + 2) seeing `keys` keys:
+    the linears 2 n L H (q + k + v + o + 3 I) and the attention 4 n keys heads dim L."""
+    c = config
+    qd, kd = c.num_attention_heads * c.head_dim, c.num_key_value_heads * c.head_dim
+    lin = 2.0 * n * c.num_hidden_layers * c.hidden_size * (qd + 2 * kd + qd + 3 * c.intermediate_size)
+    att = 4.0 * n * keys * c.num_attention_heads * c.head_dim * c.num_hidden_layers
+    return lin, att
+
+
+def cpu_velocity_baseline(config, length, frames, sample_frames=24, layers=4):
+    """The oracle's Model::velocity (scalar host build of src/model.rs:611-697) on the host
+    cores, on a bounded sample of the bench's velocity workload: `sample_frames` latent
+    frames over the same `length`-position cached prefix (seeded N(0,1) K/V), through
+    `layers` of the layers (same shapes; velocity never reads the vocabulary, so a 256-row
+    one keeps the setup short). The FLOP rate is counted like the device's; the full call's
+    time is at that rate."""
+    import copy
+    from oracle import oracle as orc
+    c = copy.copy(config)
+    c.num_hidden_layers, c.vocab_size = layers, 256
+    cores = orc.lib().orc_max_threads()
+    t0 = time.perf_counter()
+    m = orc.OracleModel.synthetic(c, seed=4, std=0.02, norm_mean=1.0, nar=True)
+    kvw = c.num_key_value_heads * c.head_dim
+    rng = np.random.default_rng(5)
+    bits = np.empty((layers, 2, length, kvw), dtype=np.uint16)
+    for li in range(layers):
+        bits[li] = rng.standard_normal((2, length, kvw), dtype=np.float32).view(np.uint32) >> 16
+    oc = m.cache(length)
+    oc.write(length, bits)
+    del bits
+    setup = time.perf_counter() - t0
+    st = rng.standard_normal((sample_frames, c.latent_dim), dtype=np.float32)
+    st = ((st.view(np.uint32).astype(np.uint64) + 0x7FFF + ((st.view(np.uint32) >> 16) & 1)) &
+          0xFFFF0000).astype(np.uint32).view(np.float32)
+    t0 = time.perf_counter()
+    m.velocity(st, oc, 0.5)
+    el = time.perf_counter() - t0
+    oc.close()
+    m.close()
+    n = sample_frames + 2
+    flop = sum(velocity_flops(c, n, length + n))
+    full = sum(velocity_flops(config, frames + 2, length + frames + 2))
+    rate = flop / el
+    return {"value": rate / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "full_call_seconds": full / rate,
+            "sample": f"one velocity call of {sample_frames} frames over the same {length}-position prefix "
+                      f"through {layers} of the {config.num_hidden_layers} layers (same shapes; {flop / 1e9:.0f} "
+                      f"GFLOP in {el:.1f} s; setup {setup:.1f} s untimed); scalar host build of the "
+                      f"reference's velocity math"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -418,10 +471,7 @@ def main():
         vms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / reps)
         assert np.isfinite(vel).all()
         n = frames + 2
-        H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
-        qd, kd = cfg.num_attention_heads * D, cfg.num_key_value_heads * D
-        lin = 2.0 * n * cfg.num_hidden_layers * H * (qd + 2 * kd + qd + 3 * I)
-        att = 4.0 * n * (length + n) * cfg.num_attention_heads * D * cfg.num_hidden_layers
+        lin, att = velocity_flops(cfg, n, length + n)
         nc.close()
         # one song through Model::synthesize: a 1,024-id prefix, 4,096 codec frames (one
         # chunk), 4 midpoint steps = 8 velocity calls, host ids in / latents out
@@ -488,6 +538,11 @@ def main():
     model.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
+        if nar:
+            try:
+                nar["cpu_baseline"] = cpu_velocity_baseline(cfg, nar["prefix_positions"], nar["frames"])
+            except Exception as e:  # the headline line must still print
+                nar["cpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"}
     dp.close()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -137,8 +137,11 @@ class OracleModel:
         return m
 
     @classmethod
-    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0):
+    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, nar=False):
+        """Seeded synthetic weights (nar: the NAR tensors too), for timing."""
         m = cls(config)
+        if nar:
+            _ck(lib().orc_model_nar(m._h, config.latent_dim, config.max_latent_frames, config.timestep_shift))
         _ck(lib().orc_model_init_synthetic(m._h, seed, std, norm_mean))
         return m
 

@@ -530,6 +530,25 @@ ORC_API int orc_model_init_synthetic(void* p, uint64_t seed, float std_, float n
     mat(L.gate, c.inter, H); mat(L.up, c.inter, H); mat(L.down, H, c.inter);
     nrm(L.in_norm, H); nrm(L.post_norm, H); nrm(L.q_norm, c.dim); nrm(L.k_norm, c.dim);
   }
+  if (m->nar_on) {  // the NAR tensors too (biases N(0, std), gains norm_mean + N(0, std))
+    auto bias = [&](std::vector<float>& b, size_t d) {
+      std::vector<uint16_t> t;
+      fill(t, d, 0.f);
+      b.resize(d);
+      for (size_t i = 0; i < d; ++i) b[i] = bf(t[i]);
+    };
+    const size_t D = m->latent;
+    mat(m->pe, m->max_frames, H);
+    mat(m->vae2llm, H, D); bias(m->vae2llm_b, H);
+    mat(m->llm2vae, D, H); bias(m->llm2vae_b, D);
+    mat(m->time_in, H, 256); bias(m->time_in_b, H);
+    mat(m->time_out, H, H); bias(m->time_out_b, H);
+    for (auto& L : m->nar) {
+      mat(L.q, qd, H); mat(L.k, kd, H); mat(L.v, kd, H); mat(L.o, H, qd);
+      mat(L.gate, c.inter, H); mat(L.up, c.inter, H); mat(L.down, H, c.inter);
+      nrm(L.in_norm, H); nrm(L.post_norm, H); nrm(L.q_norm, c.dim); nrm(L.k_norm, c.dim);
+    }
+  }
   m->ready = true;
   return 0;
 }
