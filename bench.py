@@ -353,10 +353,10 @@ def main():
         with open(prof) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
 
-    # ---- long-context sweep (config 2): decode at 4,096 and 24,576 positions
+    # ---- long-context sweep (config 2): decode at 4,096, 8,192, 16,384 and 24,576 positions
     sweep = {}
     if not args.no_sweep:
-        for L in (4096, 24576):
+        for L in (4096, 8192, 16384, 24576):
             ks = 32
             mt = 4 + ks + 1
             fill = L - 8 - mt - 1 if L == 24576 else L - 8
