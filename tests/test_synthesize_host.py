@@ -99,6 +99,18 @@ def test_oracle_synthesize_is_the_reference_loop(tiny):
     assert not np.array_equal(got, _bf16(orc.normal_tensor(99, 150, 64)))  # the ODE moved the noise
 
 
+@pytest.mark.parametrize("frames,steps", [(126, 1), (1, 2), (64, 3)])
+def test_oracle_synthesize_chunk_edges(tiny, frames, steps):
+    """Two full chunks of 63 (no remainder), a one-frame song, and one chunk plus one frame."""
+    m, c = tiny
+    rng = np.random.default_rng(frames)
+    prefix = rng.integers(0, c.vocab_size, 30).tolist()
+    codec = rng.integers(0, 32768, frames).tolist()
+    got = m.synthesize(prefix, codec, seed=frames + 1, steps=steps)
+    assert got.shape == (frames, 64)
+    assert np.array_equal(got, _synthesize(m, c, prefix, codec, frames + 1, steps))
+
+
 def test_oracle_synthesize_errors(tiny):
     m, c = tiny
     with pytest.raises(orc.OracleError):
