@@ -71,6 +71,7 @@ double logit(double t) { return std::min(20.0, std::max(-20.0, std::log(t / (1.0
 
 extern "C" int yue2_noise(uint64_t seed, uint64_t rows, uint64_t cols, float* out) {
   if (!out) return fail(YUE2_ERR_INVALID, "null argument");
+  if (cols && rows > UINT64_MAX / cols) return fail(YUE2_ERR_INVALID, "noise tensor size overflows");
   const uint64_t n = rows * cols;
   if (n < 16 || n % 16) return fail(YUE2_ERR_INVALID, "normal_tensor needs a multiple of 16 elements");
   normal_tensor(seed, n, out);
