@@ -24,6 +24,7 @@
 
 #include <array>
 #include <map>
+#include <new>
 #include <string>
 
 #include "common.cuh"
@@ -763,7 +764,11 @@ extern "C" int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uin
   if ((rc = ensure_prefill(*m))) return rc;  // the cuBLASLt state the GEMMs share
   NarBufs B;
   if ((rc = take_nar(*m, (int)n, B))) return rc;
-  rc = velocity_rows(m, c, B, state, rows, raw_t, out);
+  try {  // the host copy of the padded frames: no exception crosses the C ABI
+    rc = velocity_rows(m, c, B, state, rows, raw_t, out);
+  } catch (const std::bad_alloc&) {
+    rc = fail(YUE2_ERR_OOM, "host allocation failed");
+  }
   if (rc) cudaStreamSynchronize(m->stream);  // nothing queued may still use the block
   m->scratch_give(B.block);
   return rc;

@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -78,8 +79,8 @@ extern "C" int yue2_noise(uint64_t seed, uint64_t rows, uint64_t cols, float* ou
   return 0;
 }
 
-extern "C" int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, const int64_t* codec,
-                               uint64_t codec_len, uint64_t seed, uint64_t steps, float* out) {
+static int synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, const int64_t* codec,
+                      uint64_t codec_len, uint64_t seed, uint64_t steps, float* out) {
   const char* shape_msg = "Expected nonempty codec tokens and a 64-dimensional latent model";
   if (!m || !out || (prefix_len && !prefix) || (codec_len && !codec)) return fail(YUE2_ERR_INVALID, "null argument");
   if (!m->nar_arena) return fail(YUE2_ERR_INVALID, "NAR tensors not enabled (yue2_model_enable_nar)");
@@ -100,9 +101,13 @@ extern "C" int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t pre
     for (uint64_t i = start; i < end; ++i) ids.push_back(codec[i] + kCodecOffset);
     ids.push_back(kMusicEnd);
     // the prefill's positions plus rows + 2 latent positions for the velocity passes
-    Yue2Cache* cache = nullptr;
-    int rc = yue2_cache_create(m, ids.size() + rows + 2, &cache);
+    struct Owned {
+      Yue2Cache* c = nullptr;
+      ~Owned() { yue2_cache_free(c); }
+    } owned;
+    int rc = yue2_cache_create(m, ids.size() + rows + 2, &owned.c);
     if (rc) return rc;
+    Yue2Cache* cache = owned.c;
     rc = yue2_prefill(m, cache, ids.data(), ids.size(), YUE2_PHASE_VOCAB, nullptr);
     std::vector<float> state(noise.begin() + start * kLatent, noise.begin() + end * kLatent);
     std::vector<float> first(state.size()), mid(state.size()), vel(state.size());
@@ -114,11 +119,19 @@ extern "C" int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t pre
       if ((rc = yue2_velocity(m, cache, mid.data(), rows, logit(t - 0.5 / (double)steps), vel.data()))) break;
       for (size_t i = 0; i < state.size(); ++i) state[i] = round_bf16(state[i] - round_bf16(vel[i] * dt));
     }
-    yue2_cache_free(cache);
     if (rc) return rc;
     for (float v : state)
       if (!std::isfinite(v)) return fail(YUE2_ERR_INVALID, "Flow matching produced nonfinite latents");
     memcpy(out + start * kLatent, state.data(), state.size() * sizeof(float));
   }
   return 0;
+}
+
+extern "C" int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, const int64_t* codec,
+                               uint64_t codec_len, uint64_t seed, uint64_t steps, float* out) {
+  try {  // host vectors sized by the caller's song: no exception crosses the C ABI
+    return synthesize(m, prefix, prefix_len, codec, codec_len, seed, steps, out);
+  } catch (const std::bad_alloc&) {
+    return fail(YUE2_ERR_OOM, "host allocation failed");
+  }
 }
