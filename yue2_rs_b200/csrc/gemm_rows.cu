@@ -756,7 +756,7 @@ extern "C" int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uin
   const Geometry& g = m->g;
   const uint64_t n = rows + 2;
   if (rows == 0) return fail(YUE2_ERR_INVALID, "velocity needs at least one latent row");
-  if (c->length + n > c->capacity || c->length + n > (uint64_t)m->max_pos)
+  if (rows >= c->capacity || c->length + n > c->capacity || c->length + n > (uint64_t)m->max_pos)
     return fail(YUE2_ERR_CAPACITY, "latent rows exceed the cache/model context");
   if (!prefill_attention_supported(g)) return fail(YUE2_ERR_INVALID, "NAR velocity needs head_dim 64 or 128");
   int rc = y2_set_device(m);
