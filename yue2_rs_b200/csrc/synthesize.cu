@@ -88,7 +88,7 @@ static int synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, 
   for (uint64_t i = 0; i < codec_len; ++i)
     if (codec[i] < 0 || codec[i] >= kCodecSize) return fail(YUE2_ERR_INVALID, shape_msg);
   const uint64_t capacity = std::min<uint64_t>((uint64_t)kContext, m->cfg.max_position_embeddings);
-  if (capacity < prefix_len + 3 || (capacity - (prefix_len + 3)) / 2 == 0)
+  if (prefix_len >= capacity || capacity < prefix_len + 3 || (capacity - (prefix_len + 3)) / 2 == 0)
     return fail(YUE2_ERR_INVALID, "Prefix leaves no acoustic context");
   const uint64_t size = (capacity - (prefix_len + 3)) / 2;
   std::vector<float> noise(codec_len * kLatent);
