@@ -112,15 +112,24 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(config, steps_budget_s=20.0, threads=None):
-    """The oracle (scalar host build of the reference's decode math) on the host cores:
+def host_cores():
+    """Host threads this process may run on (its CPU affinity), whatever OMP_NUM_THREADS
+    says: torchrun sets that to 1 for every rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(config, min_tokens=120, max_s=60.0):
+    """The oracle (scalar host build of the reference's decode math) on all host cores:
     the config-1 decode step (two forwards -- cond and uncond, as sampling.rs:281-285
-    runs them -- CFG mix and choose) at a 1,024-position synthetic context, timed for
-    about `steps_budget_s` seconds."""
+    runs them -- CFG mix and choose) at a 1,024-position synthetic context, timed over
+    `min_tokens` tokens (fewer only if that takes more than `max_s` seconds). The rate is
+    one host's: the GPU count of the run does not change it."""
     from oracle import oracle as orc
     from yue2_rs_b200 import Phase
-    if threads:
-        orc.set_threads(threads)
+    orc.set_threads(host_cores())
     cores = orc.lib().orc_max_threads()
     t0 = time.perf_counter()
     m = orc.OracleModel.synthetic(config, seed=1, std=0.02)
@@ -131,10 +140,10 @@ def cpu_baseline(config, steps_budget_s=20.0, threads=None):
     caches = []
     for side in range(2):
         bits = (rng.standard_normal((c.num_hidden_layers, 2, PROMPT, kvw), dtype=np.float32).view(np.uint32) >> 16)
-        oc = m.cache(PROMPT + 64)
+        oc = m.cache(PROMPT + min_tokens + 8)
         oc.write(PROMPT, bits.astype(np.uint16))
         caches.append(oc)
-    s = c2_sampling(64)
+    s = c2_sampling(min_tokens)
     g = orc.OracleRng(1)
     tok, toks, n = 0, [], 0
     t0 = time.perf_counter()
@@ -145,13 +154,14 @@ def cpu_baseline(config, steps_budget_s=20.0, threads=None):
         toks.append(tok)
         n += 1
         el = time.perf_counter() - t0
-        if el >= steps_budget_s or n >= 60:
+        if n >= min_tokens or (el >= max_s and n >= 8):
             break
     m.close()
     return {"value": n / el, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{n} config-1 decode tokens (2 forwards + CFG mix + choose each) at a 1,024-position "
-                      f"synthetic context; weights seeded N(0,0.02) (setup {setup:.1f}s untimed); scalar host build "
-                      f"of the reference decode math, not Accelerate"}
+                      f"synthetic context in {el:.1f} s on {cores} host threads; weights seeded N(0,0.02) (setup "
+                      f"{setup:.1f}s untimed); scalar host build of the reference decode math, not Accelerate; "
+                      f"one host's rate, independent of the run's GPU count"}
 
 
 def velocity_flops(config, n, keys):
@@ -212,7 +222,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     from yue2_rs_b200 import synth
-    cb = cpu_baseline(synth.config_c2(), steps_budget_s=max(5.0, min(25.0, 3.0 * args.steps)))
+    cb = cpu_baseline(synth.config_c2())
     line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -357,7 +367,7 @@ def main():
     sweep = {}
     if not args.no_sweep:
         for L in (4096, 8192, 16384, 24576):
-            ks = 32
+            ks = 128  # config 2: 128 timed decode steps at each length
             mt = 4 + ks + 1
             fill = L - 8 - mt - 1 if L == 24576 else L - 8
             r = Request(cond[:8], seed=rank, negative=uncond[:8], scale=SCALE, context_fill=fill)

@@ -293,7 +293,7 @@ void yue2_session_free(Yue2Session* ss);
 /* Measurement hook (no reference counterpart): `launches` back-to-back launches of one
  * weight-streaming GEMV kind over the layers in turn, `rows` activation rows, CUDA
  * events on the model's stream. kind 0 = gate|up + SwiGLU, 1 = q|k|v, 2 = down +
- * residual, 3 = final norm + LM head. Returns the mean launch time and the weight
+ * residual, 3 = final norm + LM head, 4 = o + residual. Returns the mean launch time and the weight
  * bytes one launch streams. */
 int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, double* avg_ms, double* bytes);
 

@@ -32,3 +32,13 @@ def test_cpu_velocity_baseline_runs(bench):
     assert r["unit"] == "TFLOP/s" and r["kind"] == "port" and r["value"] > 0
     assert r["full_call_seconds"] > 0 and r["cores"] >= 1
     assert "200-position prefix" in r["sample"]
+
+
+def test_cpu_baseline_uses_every_host_core_under_torchrun(bench, monkeypatch):
+    """torchrun sets OMP_NUM_THREADS=1 for each rank; the CPU baseline still runs on all the
+    cores the process may use, so its rate is the same at every GPU count."""
+    monkeypatch.setenv("OMP_NUM_THREADS", "1")
+    r = bench.cpu_baseline(synth.config_c1(), min_tokens=3)
+    assert r["cores"] == bench.host_cores()
+    assert r["kind"] == "port" and r["value"] > 0
+    assert "3 config-1 decode tokens" in r["sample"]

@@ -2,6 +2,8 @@
 (metal.m:686-706) against the reference's golden test (src/tensor.rs:7-83)."""
 import ctypes
 import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -73,3 +75,19 @@ def test_vector_dropin_matches_f64():
         scale = np.abs(wf) @ np.abs(x.astype(np.float64))
         assert np.all(np.abs(out - want) <= 1e-5 * scale + 1e-6)
     L.yue2_cuda_clear_weights()
+
+
+def test_pipelined_loops_match_reference_golden():
+    """The golden and short-context cases above on the pipelined tile loops: tensor-core
+    scores and P.V (attn_mma_kernel) at dims 64 and 128, the SIMT pipelined loop at 256.
+    YUE2_CUDA_ATTN_PIPE=1 forces them for every length (the engine itself picks them from
+    about 1.5 tiles per warp: 24,576 keys here, 4k positions for a CFG pair); the switch is
+    read once per process, so the cases rerun in a child process."""
+    if os.environ.get("YUE2_CUDA_ATTN_PIPE"):
+        pytest.skip("this process already runs with the switch set")
+    env = dict(os.environ, YUE2_CUDA_ATTN_PIPE="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", os.path.abspath(__file__),
+                        "-m", "gpu", "-k", "matches_reference_golden or short_contexts"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert "4 passed" in r.stdout, r.stdout[-2000:]

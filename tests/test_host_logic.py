@@ -77,3 +77,14 @@ def test_synthetic_checkpoint_is_deterministic():
     assert "model.layers.0.nar_mlp.down_proj.weight" in a and "latent_pos_embed.pe" in a
     g = a["model.layers.0.input_layernorm.weight"].astype(np.uint32) << 16
     assert np.allclose(g.view(np.float32), 1.0, atol=0.1)
+
+
+def test_noalloc_attention_rejects_overflowing_shapes_before_any_launch():
+    """Shape values whose products would wrap 64 bits are refused up front (no device
+    call is made, so this runs without a GPU)."""
+    L = _lib.lib()
+    p = 256  # aligned, never dereferenced: the shape check comes first
+    kv = (1 << 62) + 1
+    for heads, kvh in ((2 * kv, kv), (1 << 40, 1), (4, 70000)):
+        assert L.yue2_attention_noalloc(p, p, p, p, 64, heads, kvh, 128, None) == -1
+        assert "invalid attention shape" in _lib.last_error()

@@ -26,14 +26,16 @@ def bits(a):
     return (np.ascontiguousarray(a, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
 
 
-@pytest.mark.parametrize("dim,keys", [(128, 4097), (64, 24576), (256, 333)])
-def test_noalloc_attention_matches_existing_entry_point(dim, keys):
+# (heads, kv): the reference test's 4/2 (G=2), the reduced model's 8/2 (G=4) and the
+# 3B-shaped model's 24/8 (G=3)
+@pytest.mark.parametrize("dim,keys,heads,kv", [(128, 4097, 4, 2), (64, 24576, 4, 2), (256, 333, 4, 2),
+                                               (128, 4097, 8, 2), (128, 2049, 24, 8), (128, 24576, 24, 8)])
+def test_noalloc_attention_matches_existing_entry_point(dim, keys, heads, kv):
     import torch
     L = _lib.lib()
-    heads, kv = 4, 2
     q, k, v = attention_inputs(heads, kv, dim, keys - 1, 1)  # the reference inputs with one appended key
     want = np.empty(heads * dim, dtype=np.float32)
-    cache = 777000 + dim * 100000 + keys
+    cache = 777000 + dim * 100000 + keys + heads * 10_000_000
     assert L.yue2_cuda_cached_attention(_p(q), _p(k), _p(v), _p(want), k.shape[0], heads, kv, dim, cache, 0) == 1, \
         _lib.last_error()
     L.yue2_cuda_release_cache(cache)

@@ -409,6 +409,7 @@ int yue2_cuda_cached_attention(const float* q, const float* k, const float* v, f
   ap.layer = 0;
   ap.splits = std::max(1, std::min(64, (2 * d.sms + (int)kv - 1) / (int)kv));
   ap.scale = 1.0f / sqrtf((float)dim);
+  ap.pipe = attn_pipe_for_keys((int)keys, ap.splits);  // the engine's choice of tile loop
   if (!ok_or(launch_attention(d.stream, false, ap, 1), "attention launch")) return 0;
   std::vector<uint16_t> ob(heads * dim);
   if (!ok_or(cudaMemcpyAsync(ob.data(), d.attn, ob.size() * 2, cudaMemcpyDeviceToHost, d.stream), "output") ||

@@ -588,15 +588,18 @@ int yue2_cache_read(const Yue2Cache* c, uint64_t layer, uint64_t begin, uint64_t
   int rc = y2_set_device(c->m);
   if (rc) return rc;
   const size_t D = g.dim, kd = (size_t)g.kvh * D;
-  std::vector<uint16_t> tmp(D);
-  for (uint64_t t = begin; t < begin + count; ++t) {
-    const char* page = (const char*)c->pages[t / kPageTokens];
-    for (int h = 0; h < g.kvh; ++h)
-      for (int kvsel = 0; kvsel < 2; ++kvsel) {
-        const size_t off = (kv_offset(g, (int)layer, kvsel, h) + (t % kPageTokens) * D) * 2;
-        CK(cudaMemcpy(tmp.data(), page + off, D * 2, cudaMemcpyDeviceToHost));
-        memcpy((kvsel ? v : k) + (t - begin) * kd + h * D, tmp.data(), D * 2);
-      }
+  // one copy per page: the layer's K and V blocks are adjacent ([K|V][kv head][64][dim])
+  const size_t block = 2 * (size_t)g.kvh * kPageTokens * D;
+  std::vector<uint16_t> tmp(block);
+  for (uint64_t t = begin; t < begin + count;) {
+    const uint64_t pg = t / kPageTokens, end = std::min<uint64_t>(begin + count, (pg + 1) * kPageTokens);
+    const char* page = (const char*)c->pages[pg];
+    CK(cudaMemcpy(tmp.data(), page + kv_offset(g, (int)layer, 0, 0) * 2, block * 2, cudaMemcpyDeviceToHost));
+    for (; t < end; ++t)
+      for (int h = 0; h < g.kvh; ++h)
+        for (int kvsel = 0; kvsel < 2; ++kvsel)
+          memcpy((kvsel ? v : k) + (t - begin) * kd + h * D,
+                 tmp.data() + kv_offset(g, 0, kvsel, h) + (t % kPageTokens) * D, D * 2);
   }
   return 0;
 }
@@ -908,11 +911,7 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
   return launch_step_end(s, pdl, m.rows, R);
 }
 
-// The pipelined attention loop pays off once a warp streams about 1.5 tiles of 32 keys or
-// more (measured at two rows: +1.3% at 4k positions, +3.5% at 24k, -1.2% at 1k).
-int attn_pipe_for(const Yue2Model& m, int R) {
-  return 2 * (int64_t)m.ctx_hint >= 3 * 32 * 4 * (int64_t)splits_for(m, R) ? 1 : 0;
-}
+int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
   if (head && m.step_plans.count(R * 16 + phase)) return 1 + (phase != kPhaseVocab) + 1;
@@ -1146,12 +1145,21 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
         p.of = m->x;
         p.ldo = H;
         return launch_gemv(m->stream, false, kXBf16, kEpiResidual, p, m->gemv_grid);
+      case 4:  // o + residual
+        p.w[0] = p.w[1] = p.w[2] = w.o;
+        p.seg_start[1] = p.seg_start[2] = p.N = H;
+        p.K = qd;
+        p.xb = m->attn;
+        p.of = m->x;
+        p.ldo = H;
+        return launch_gemv(m->stream, false, kXBf16, kEpiResidual, p, m->gemv_grid);
       default:  // LM head
         return encode_head(*m, m->stream, false, 0, rows, 0, kPhaseVocab, nullptr);
     }
   };
   const double per_row_bytes = kind == 0 ? 2.0 * I * H * 2 : kind == 1 ? (double)(qd + 2 * kd) * H * 2
-                               : kind == 2 ? (double)H * I * 2 : (double)g.vocab * H * 2;
+                               : kind == 2 ? (double)H * I * 2 : kind == 4 ? (double)H * qd * 2
+                                                                           : (double)g.vocab * H * 2;
   for (int i = 0; i < 3; ++i) CK(one(i % g.layers));
   cudaEvent_t a, b;
   CK(cudaEventCreate(&a));

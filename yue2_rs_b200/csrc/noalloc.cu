@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <mutex>
 #include <string>
 
@@ -278,7 +279,10 @@ extern "C" int yue2_attention_noalloc(const uint16_t* q, const uint16_t* k, cons
   if (!q || !k || !v || !out) return fail(YUE2_ERR_INVALID, "null device pointer");
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15)
     return fail(YUE2_ERR_INVALID, "q, k, v and out must be 16-byte aligned device pointers");
-  if (keys == 0 || keys > (1u << 30) || heads == 0 || kv == 0 || heads % kv)
+  // bounds before any arithmetic on the caller's sizes: kv is the grid's y extent (at most
+  // 65,535), and heads must fit the kernel's int arguments
+  if (keys == 0 || keys > (1u << 30) || heads == 0 || kv == 0 || kv > 65535 || heads > (uint64_t)INT32_MAX ||
+      heads % kv)
     return fail(YUE2_ERR_INVALID, "invalid attention shape");
   if (dim != 64 && dim != 128 && dim != 256) return fail(YUE2_ERR_INVALID, "head dim must be 64, 128 or 256");
   const uint64_t groups = heads / kv;

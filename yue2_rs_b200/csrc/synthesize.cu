@@ -85,6 +85,7 @@ static int synthesize(Yue2Model* m, const int64_t* prefix, uint64_t prefix_len, 
   if (!m || !out || (prefix_len && !prefix) || (codec_len && !codec)) return fail(YUE2_ERR_INVALID, "null argument");
   if (!m->nar_arena) return fail(YUE2_ERR_INVALID, "NAR tensors not enabled (yue2_model_enable_nar)");
   if ((uint64_t)m->nar.latent != kLatent || codec_len == 0 || steps == 0) return fail(YUE2_ERR_INVALID, shape_msg);
+  if (codec_len > SIZE_MAX / (kLatent * sizeof(float))) return fail(YUE2_ERR_INVALID, "codec length too large");
   for (uint64_t i = 0; i < codec_len; ++i)
     if (codec[i] < 0 || codec[i] >= kCodecSize) return fail(YUE2_ERR_INVALID, shape_msg);
   const uint64_t capacity = std::min<uint64_t>((uint64_t)kContext, m->cfg.max_position_embeddings);
@@ -133,5 +134,7 @@ extern "C" int yue2_synthesize(Yue2Model* m, const int64_t* prefix, uint64_t pre
     return synthesize(m, prefix, prefix_len, codec, codec_len, seed, steps, out);
   } catch (const std::bad_alloc&) {
     return fail(YUE2_ERR_OOM, "host allocation failed");
+  } catch (const std::exception& e) {  // e.g. std::length_error from a vector size
+    return fail(YUE2_ERR_INVALID, std::string("host error: ") + e.what());
   }
 }
