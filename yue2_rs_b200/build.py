@@ -18,7 +18,7 @@ OUT = os.path.join(HERE, "libyue2cuda.so")
 BUILD = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["kernels_layer.cu", "kernels_gemv.cu", "kernels_step.cu", "kernels_sample.cu", "gemm_rows.cu", "kernels_gemm_tc.cu", "kernels_prefill_attn.cu", "kernels_prefill_attn_tc.cu", "engine.cu", "engine_sample.cu", "checkpoint.cu", "dropin.cu", "noalloc.cu", "synthesize.cu"]
+SOURCES = ["kernels_layer.cu", "kernels_gemv.cu", "kernels_sample.cu", "gemm_rows.cu", "kernels_gemm_tc.cu", "kernels_prefill_attn.cu", "kernels_prefill_attn_tc.cu", "engine.cu", "engine_sample.cu", "checkpoint.cu", "dropin.cu", "noalloc.cu", "synthesize.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off,-O2",
                 "-I" + CSRC, "-I" + INCLUDE]
@@ -69,7 +69,7 @@ def build(force=False, verbose=True):
                     print("compiled", os.path.relpath(o, HERE), flush=True)
     if force or jobs or _stale(OUT, objs):
         cmd = [nvcc()] + ARCH + ["-shared", "-o", OUT + ".tmp"] + objs + ["-lcuda", "-lcublasLt",
-                                                           "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+                                                           "-Xlinker", "-rpath=/usr/local/cuda/lib64", "-Xlinker", "--no-undefined"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

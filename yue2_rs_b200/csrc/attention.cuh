@@ -1,5 +1,5 @@
-// Decode attention and the QK norm + RoPE of one head, shared by the standalone kernels
-// (kernels_layer.cu) and the persistent decode-step kernel (kernels_step.cu).
+// Decode attention and the QK norm + RoPE of one head, used by the decode attention kernels
+// (kernels_layer.cu) and the no-alloc entry point (noalloc.cu).
 #pragma once
 #include <cuda_runtime.h>
 
@@ -43,22 +43,19 @@ Y2_DEV void norm_rope_head(const uint16_t* src, const float* gamma, float eps, c
 // accumulates P.V with lanes over head dims. Warps merge in shared memory; splits
 // merge through f32 partials, and the last split CTA to finish (atomic ticket; no
 // waiting) normalises and writes the bf16 output.
-// 128-thread barrier: the attention body runs on the whole CTA of attn_kernel, or on
-// warps 0-3 of a larger CTA (the persistent step kernel).
+// 128-thread barrier of the attention CTA.
 Y2_DEV void attn_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// One (split, kv head, row) item of split-K decode attention on warps 0-3 of the calling
-// CTA. STANDALONE: the attn_kernel launch (programmatic dependent launch, first tile
-// requested before the wait, splits merged by the last CTA through an atomic ticket).
-// Otherwise the caller runs after a grid-wide barrier and merges the partials itself
-// after another one (attn_merge_slice). PIPE (passes of many rows, each CTA streaming
+// One (split, kv head, row) item of split-K decode attention: one CTA of four warps, a
+// programmatic dependent launch (the first tile requested before the wait), splits merged by
+// the last CTA through an atomic ticket. PIPE (passes of many rows, each CTA streaming
 // many tiles per warp): two K buffers per warp; the next tile's K is requested before the
 // current tile's scores and its V right after the current P.V, so loads overlap compute.
 // MMA (implies PIPE; G <= 8, D <= 128): scores and P.V on the tensor cores. The G query
 // heads are the rows of one m16n8k16 A tile (bf16; q is already bf16-exact), a 32-key K
 // tile gives four n-tiles, and P.V multiplies P split into bf16 hi + lo parts so that the
 // probabilities keep f32 accuracy. V rows past the last key are zero-filled.
-template <int D, int G, bool STANDALONE, bool PIPE = false, bool MMA = false>
+template <int D, int G, bool PIPE = false, bool MMA = false>
 Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned char* smem_raw) {
   static_assert(!MMA || (PIPE && G <= 8 && D <= 128), "tensor-core attention shape");
   constexpr int CPR = D / 8;  // 16-byte chunks per key row
@@ -109,7 +106,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   // the tile holding the new position is written in this launch (fused) or by the
   // preceding kernel (prefill rows): it is never fetched before the wait
   const int first_tile = t0 + warp;
-  const bool early = STANDALONE && a.fused && first_tile < t1 && first_tile != ntiles - 1;
+  const bool early = a.fused && first_tile < t1 && first_tile != ntiles - 1;
   // PIPE: K (swizzled) of tile t into buffer buf, V of tile t; one commit group each. The
   // page base comes from the caller (fetched a tile ahead, off the issue path).
   auto page_of = [&](int t) { return reinterpret_cast<const uint16_t*>(row.pages[(t << 5) >> kPageLog2]); };
@@ -148,10 +145,8 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
   }
 
-  if (STANDALONE) {
-    pdl_wait();
-    pdl_trigger();
-  }
+  pdl_wait();
+  pdl_trigger();
 
   if (a.fused) {
     const int pos = row.pos;
@@ -472,7 +467,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
       ph[2 + d] = O;
     }
   }
-  if (nsplit == 1 || !STANDALONE) return;
+  if (nsplit == 1) return;
   __threadfence();
   attn_sync();
   if (threadIdx.x == 0) s_ticket = atomicAdd(a.counters + r * geo.kvh + g, 1);

@@ -272,7 +272,6 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   m->gemv_grid = m->sms * std::max(1, env_int("YUE2_CUDA_GEMV_CTAS_PER_SM", 2));
   m->use_pdl = env_int("YUE2_CUDA_PDL", 1) != 0;
   m->use_graphs = env_int("YUE2_CUDA_GRAPHS", 1) != 0;
-  m->use_step = env_int("YUE2_CUDA_STEP", 0) != 0;
   {
     const char* v = getenv("YUE2_CUDA_PREFILL");
     m->use_prefill_gemm = !(v && std::string(v) == "gemv");
@@ -678,8 +677,7 @@ cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float
   return launch_gemv(s, pdl, kXNorm, kEpiLogits, p, m.gemv_grid);
 }
 
-// Parameters of layer l's kernels for R rows (shared by the kernel chain and the
-// persistent step kernel's plan).
+// Parameters of layer l's kernels for R rows.
 struct LayerOps {
   GemvParams qkv, o, gu, down;
   RopeParams rope;
@@ -790,103 +788,8 @@ static LayerOps layer_ops(const Yue2Model& m, int l, int R, bool fused, const in
   return op;
 }
 
-// ---- persistent step kernel: eligibility, plan (device descriptors) and launch
-static bool step_eligible(const Yue2Model& m, int R) {
-  const Geometry& g = m.g;
-  const int G = g.heads / g.kvh;
-  if (!m.use_step || R > 2 || g.dim != 128 || !(G == 1 || G == 2 || G == 3 || G == 4 || G == 8)) return false;
-  const int qd = g.heads * g.dim;
-  if (g.hidden % 256 || g.inter % 256 || qd % 256) return false;
-  const int max_k = std::max(std::max(g.hidden, g.inter), qd);
-  return step_kernel_smem(g.dim, G, R, max_k) <= 227 * 1024 - 1024 - 1024;
-}
-
-static int step_splits(const Yue2Model& m, int R) { return std::max(1, std::min(m.max_splits, m.sms / (m.g.kvh * R))); }
-
-// Builds (once, outside any stream capture) the device descriptors of the step kernel.
-int prepare_step_plan(Yue2Model& m, int R, int phase) {
-  if (!step_eligible(m, R)) return 0;
-  const int key = R * 16 + phase;
-  if (m.step_plans.count(key)) return 0;
-  const Geometry& g = m.g;
-  const int L = g.layers, S = step_splits(m, R);
-  std::vector<StepGemv> ph(4 * L + 1);
-  std::vector<AttnParams> at(L);
-  for (int l = 0; l < L; ++l) {
-    const LayerOps op = layer_ops(m, l, R, true, nullptr, S);
-    ph[4 * l + 0] = StepGemv{op.qkv, kXNorm, kEpiBf16, 0};
-    ph[4 * l + 1] = StepGemv{op.o, kXBf16, kEpiResidual, 0};
-    ph[4 * l + 2] = StepGemv{op.gu, kXNorm, kEpiSwiGLU, 1};
-    ph[4 * l + 3] = StepGemv{op.down, kXBf16, kEpiResidual, 0};
-    at[l] = op.attn;
-  }
-  GemvParams hp = {};
-  hp.error = m.flags + 2;
-  head_params(m, phase, hp);
-  hp.K = g.hidden;
-  hp.R = R;
-  hp.xf = m.x;
-  hp.gamma = m.final_norm;
-  hp.eps = g.eps;
-  hp.of = m.logits;
-  hp.ldo = g.vocab;
-  ph[4 * L] = StepGemv{hp, kXNorm, kEpiLogits, 0};
-  Yue2Model::StepPlan plan;
-  void* p = nullptr;
-  int rc;
-  if ((rc = m.alloc(&p, ph.size() * sizeof(StepGemv)))) return rc;
-  plan.phases = (StepGemv*)p;
-  if ((rc = m.alloc(&p, at.size() * sizeof(AttnParams)))) return rc;
-  plan.attn = (AttnParams*)p;
-  if ((rc = m.alloc(&p, 256))) return rc;
-  plan.barrier = (unsigned*)p;
-  CK(cudaMemcpy(plan.phases, ph.data(), ph.size() * sizeof(StepGemv), cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(plan.attn, at.data(), at.size() * sizeof(AttnParams), cudaMemcpyHostToDevice));
-  CK(cudaMemset(plan.barrier, 0, 256));
-  StepParams sp = {};
-  const int G = g.heads / g.kvh;
-  const int max_k = std::max(std::max(g.hidden, g.inter), g.heads * g.dim);
-  sp.smem = step_kernel_smem(g.dim, G, R, max_k);
-  if (launch_step(nullptr, sp, g.dim, G, m.sms, true) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;  // the shape does not fit the kernel: decode keeps the kernel chain
-  }
-  m.step_plans[key] = plan;
-  return 0;
-}
-
-static cudaError_t encode_step(Yue2Model& m, cudaStream_t s, int R, int phase, const int32_t* skip) {
-  const Geometry& g = m.g;
-  const Yue2Model::StepPlan& plan = m.step_plans.at(R * 16 + phase);
-  cudaError_t e;
-  if (phase != kPhaseVocab && (e = launch_fill_f32(s, m.logits, (size_t)R * g.vocab, -INFINITY)) != cudaSuccess)
-    return e;
-  if ((e = cudaMemsetAsync(plan.barrier, 0, 4, s)) != cudaSuccess) return e;
-  StepParams sp = {};
-  sp.phases = plan.phases;
-  sp.attn = plan.attn;
-  sp.layers = g.layers;
-  sp.R = R;
-  sp.rows = m.rows;
-  sp.embed = m.embed;
-  sp.hidden = g.hidden;
-  sp.vocab = g.vocab;
-  sp.x = m.x;
-  sp.tok_error = m.flags + 0;
-  sp.barrier = plan.barrier;
-  sp.stall = m.flags + 2;
-  sp.skip = skip;
-  const int G = g.heads / g.kvh;
-  const int max_k = std::max(std::max(g.hidden, g.inter), g.heads * g.dim);
-  sp.smem = step_kernel_smem(g.dim, G, R, max_k);
-  if ((e = launch_step(s, sp, g.dim, G, m.sms, false)) != cudaSuccess) return e;
-  return launch_step_end(s, m.use_pdl, m.rows, R);
-}
-
-// embed -> layers -> [final norm + LM head] -> position advance, as one PDL chain (or, for
-// decode steps the persistent step kernel covers, one cooperative launch).
+// embed -> layers -> [final norm + LM head] -> position advance, as one PDL chain.
 cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip) {
-  if (head && m.step_plans.count(R * 16 + phase)) return encode_step(m, s, R, phase, skip);
   const Geometry& g = m.g;
   const bool pdl = m.use_pdl;
   cudaError_t e = launch_embed(s, pdl, m.rows, R, m.embed, g.hidden, g.vocab, m.x, m.flags + 0);
@@ -914,7 +817,6 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
-  if (head && m.step_plans.count(R * 16 + phase)) return 1 + (phase != kPhaseVocab) + 1;
   return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1;
 }
 
@@ -927,10 +829,6 @@ int run_forward(Yue2Model& m, int R, bool head, int phase) {
   }
   auto it = m.graphs.find(key);
   if (it == m.graphs.end()) {
-    if (head) {
-      const int rc = prepare_step_plan(m, R, phase);
-      if (rc) return rc;
-    }
     cudaGraph_t graph;
     CK(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = encode_forward(m, m.stream, R, head, phase, nullptr);

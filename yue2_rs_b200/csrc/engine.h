@@ -45,14 +45,7 @@ struct Yue2Model {
   int sms = 148;
   int gemv_grid = 148;
   bool use_pdl = true, use_graphs = true;
-  bool use_step = false;  // persistent decode-step kernel for R <= 2 (YUE2_CUDA_STEP=1)
   int ctx_hint = 0;       // longest row context of the next captured forward (picks the attention loop)
-  struct StepPlan {
-    y2::StepGemv* phases = nullptr;
-    y2::AttnParams* attn = nullptr;
-    unsigned* barrier = nullptr;
-  };
-  std::map<int, StepPlan> step_plans;  // key R * 16 + phase
   bool use_prefill_gemm = true;  // prompts of >= kPrefillGemmMin ids as GEMMs (YUE2_CUDA_PREFILL=gemv: off)
   int prefill_chunk = 1024;      // rows per GEMM prefill chunk, <= kPrefillRows (YUE2_CUDA_PREFILL_CHUNK)
   bool prefill_tc_attn = true;   // tensor-core prefill attention (YUE2_CUDA_PREFILL_ATTN=rows: per-row kernel)
@@ -152,7 +145,6 @@ cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float
                              const int32_t* skip);
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
 int attn_pipe_for(const Yue2Model& m, int R);
-int prepare_step_plan(Yue2Model& m, int R, int phase);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
 int take_flags(Yue2Model& m);

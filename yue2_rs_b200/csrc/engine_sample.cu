@@ -420,7 +420,6 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
 
   // ---- decode step graph: forward(R rows) || MT words, then sample
   if (s->max_tokens > 1) {
-    if (!wide && (rc = prepare_step_plan(*m, R, phase))) return bail(rc);
     if (wide && (rc = prepare_wide(*m, R, phase))) return bail(rc);
     m->ctx_hint = 0;
     for (int r = 0; r < R; ++r) m->ctx_hint = std::max(m->ctx_hint, (int)rows[r].pos + 1);

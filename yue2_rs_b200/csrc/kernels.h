@@ -172,28 +172,6 @@ struct SampleParams {
   SampleAcc* acc;          // [nreq], {0, 0, ~0} between steps
 };
 
-// ---- persistent decode step (kernels_step.cu)
-struct StepGemv {  // one GEMV phase of the step: parameters plus the template choices
-  GemvParams p;
-  int xmode, epi, pair;
-};
-struct StepParams {
-  const StepGemv* phases;  // [4 * layers + 1]: per layer q|k|v, o, gate|up, down; then the LM head
-  const AttnParams* attn;  // [layers]
-  int layers, R;
-  DevRow* rows;
-  const uint16_t* embed;
-  int hidden, vocab;
-  float* x;                // residual stream [R, hidden]
-  int32_t* tok_error;
-  unsigned* barrier;       // grid-barrier arrival counter, zero at launch
-  int32_t* stall;          // set to 1 when a bounded barrier wait gives up
-  const int32_t* skip;     // optional: the whole launch is skipped when *skip != 0
-  size_t smem;
-};
-size_t step_kernel_smem(int dim, int groups, int R, int max_k);
-cudaError_t launch_step(cudaStream_t s, const StepParams& p, int dim, int groups, int sms, bool configure_only);
-
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const uint16_t* embed, int hidden,
                          int vocab, float* x, int32_t* error);

@@ -454,21 +454,21 @@ cudaError_t launch_rope_append(cudaStream_t s, bool pdl, const RopeParams& p, in
 template <int D, int G>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnParams a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  attn_item<D, G, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+  attn_item<D, G>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
 }
 
 // Passes of more than kMaxRows rows: the pipelined tile loop.
 template <int D, int G>
 __global__ void __launch_bounds__(128) attn_pipe_kernel(const AttnParams a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  attn_item<D, G, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+  attn_item<D, G, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
 }
 
 // The pipelined loop with scores and P.V on the tensor cores (dim <= 128).
 template <int D, int G>
 __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  attn_item<D, G, true, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
+  attn_item<D, G, true, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, smem_raw);
 }
 
 static int attention_smem_need(int dim, int groups, bool pipe = false, bool mma = false) {
