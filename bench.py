@@ -234,6 +234,58 @@ def run_reference(args):
     return 0
 
 
+def run_tp(args, dp, local):
+    """the 3B-shaped model split over the world's ranks (heads, MLP rows and
+    LM-head vocabulary rows; peer-memory exchanges after o, down and the head), one song with
+    CFG 1.5 at a 4,096-position context (seeded N(0,1) KV fill ahead of 2-id prompts), 256
+    decode steps, each timed alone with CUDA events on the session's stream. world 1 is the
+    unsharded model on the same workload."""
+    import torch
+    from yue2_rs_b200 import Model, Phase, Request, Session, synth, tp
+    rank, world = dp.rank, dp.world
+    cfg = synth.config_c2()
+    model = Model.synthetic(cfg, seed=1, std=0.02, device=local, tp=(rank, world) if world > 1 else None)
+    if world > 1:
+        tp.connect(model, dp.group if hasattr(dp, "group") else None)
+    steps, W = 256, max(args.warmup, 3)
+    ctx = 4096
+    cond, uncond = prompts(1000, cfg.vocab_size)
+    req = Request(cond[:2], seed=7, negative=uncond[:2], scale=SCALE, context_fill=ctx - 2)
+    sess = Session(model, [req], c2_sampling(W + steps + 1), Phase.VOCAB)
+    st = torch.cuda.ExternalStream(sess.cuda_stream)
+    sess.step(W)
+    sess.sync()
+    dp.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record(st)
+    for i in range(steps):
+        sess.step(1)
+        ev[i + 1].record(st)
+    sess.sync()
+    dp.barrier()
+    clk = clocks.stop()
+    per = np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(steps)])
+    toks, _ = sess.collect()[0]
+    sess.close()
+    model.close()
+    p50, p99, total = dp.max(float(np.percentile(per, 50))), dp.max(float(np.percentile(per, 99))), dp.max(float(per.sum()))
+    line = {"metric": "single-song per-token decode latency (BASELINE config 5)", "tp": world, "n_gpus": world,
+            "p50_ms": p50, "p99_ms": p99, "mean_ms": total / steps, "tokens_per_s": steps / (total / 1000.0),
+            "unit": "ms", "higher_is_better": False, "steps": steps, "warmup": W, "tokens": len(toks),
+            "config": {"workload": "config 5: 3B-shaped AR decode, CFG 1.5, T1.0/top-k50/top-p0.93, 4,096-position "
+                                   "context (seeded KV fill + 2-id prompts), one song",
+                       "parallelism": f"tp{world}: q|k|v and gate|up by output rows, o and down by input columns, "
+                                      "LM head by vocabulary rows; peer-memory all-reduce after o and down, "
+                                      "all-gather after the head" if world > 1 else "tp1 (unsharded)"},
+            "clocks": clk, "data": "synthetic"}
+    dp.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -256,6 +308,9 @@ def main():
     ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
                     help="one N-id prefill of the config-1 model and exit: the command line for the "
                          "prefill's ncu launch list")
+    ap.add_argument("--tp", action="store_true",
+                    help="BASELINE config 5: one song's decode split over the torchrun ranks (tensor "
+                         "parallel), 4,096-position context, 256 steps; per-token latency p50/p99")
     ap.add_argument("--velocity-profile", type=int, default=0, metavar="F",
                     help="one Model::velocity call of F latent frames after a synthetic 1,025-position "
                          "prefix (3B-shaped NAR model; --profile-layers N for a smaller one) and exit")
@@ -279,6 +334,8 @@ def main():
     def max_over_ranks(x):
         return dp.max(x)
 
+    if args.tp:
+        return run_tp(args, dp, local)
     cfg = synth.config_c2()
     if (args.profile or args.velocity_profile) and args.profile_layers > 0:
         cfg.num_hidden_layers = args.profile_layers

@@ -145,6 +145,25 @@ typedef struct {
 /* Model::open (src/model.rs:418-451) without file IO: allocate device storage for the
  * AR tensors of `cfg` on `device`. Tensors arrive through yue2_model_set_tensor. */
 int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out);
+/* Tensor parallelism (no counterpart in the reference, which runs on one device; the
+ * optional split of BASELINE's single-song latency configuration). Rank `tp_rank` of
+ * `tp_world` (at most 8, one process per GPU) holds heads / world query and KV heads (its
+ * own KV cache), intermediate / world MLP rows, the matching input columns of o_proj and
+ * down_proj, and its share of the LM-head vocabulary rows; the embedding and the RMSNorm
+ * gains are whole. yue2_model_init_synthetic fills a shard with exactly the values the
+ * unsharded model holds at those positions; yue2_model_set_tensor takes the shard's own
+ * slice (the checkpoint loader refuses a sharded model). After yue2_model_finalize every
+ * rank calls yue2_tp_export, the ranks exchange the handles (any host channel), and every
+ * rank calls yue2_tp_connect with all of them in rank order. Decode (forward, prefill,
+ * sessions, generate) then runs one or two rows per pass, every rank the same calls in the
+ * same order; o and down end in an exchange that sums the ranks' partials in rank order and
+ * applies the residual, and the LM head ends in a gather of the vocabulary slices, so every
+ * rank holds identical logits and samples identical tokens. */
+int yue2_model_create_tp(int device, const Yue2Config* cfg, uint64_t tp_rank, uint64_t tp_world, Yue2Model** out);
+/* 128 bytes: this rank's two CUDA IPC handles (exchange buffer, logits). */
+int yue2_tp_export(Yue2Model* m, void* handles);
+/* tp_world x 128 bytes of handles in rank order (this rank's own entry is not opened). */
+int yue2_tp_connect(Yue2Model* m, const void* handles);
 /* Upload one checkpoint tensor by its reference name (model.rs:76-93,103-114,176-200,
  * 250-270,418-451). Tensors outside the AR decode path are accepted and ignored (returns 1). */
 int yue2_model_set_tensor(Yue2Model* m, const char* name, int dtype, const void* data, uint64_t rows,

@@ -86,6 +86,9 @@ _PROTOS = {
     "yue2_cuda_cached_attention": (c_int, [c_p, c_p, c_p, c_p, c_size, c_size, c_size, c_size, c_size, c_size]),
     "yue2_attention_noalloc": (c_int, [c_p, c_p, c_p, c_p, c_u64, c_u64, c_u64, c_u64, c_p]),
     "yue2_model_create": (c_int, [c_int, ctypes.POINTER(Config), ctypes.POINTER(c_p)]),
+    "yue2_model_create_tp": (c_int, [c_int, ctypes.POINTER(Config), c_u64, c_u64, ctypes.POINTER(c_p)]),
+    "yue2_tp_export": (c_int, [c_p, c_p]),
+    "yue2_tp_connect": (c_int, [c_p, c_p]),
     "yue2_model_set_tensor": (c_int, [c_p, ctypes.c_char_p, c_int, c_p, c_u64, c_u64]),
     "yue2_model_init_synthetic": (c_int, [c_p, c_u64, c_f, c_f]),
     "yue2_model_finalize": (c_int, [c_p]),

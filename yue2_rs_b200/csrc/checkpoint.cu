@@ -404,6 +404,8 @@ int yue2_checkpoint_scan(const char* dir, uint64_t* tensors) {
 }
 
 int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_uploaded) {
+  if (m && m->tp_world > 1)
+    return fail(YUE2_ERR_INVALID, "a tensor-parallel model takes its shard through yue2_model_set_tensor");
   if (!m || !dir) return fail(YUE2_ERR_INVALID, "null argument");
   std::map<std::string, Entry> entries;
   int rc = scan_checkpoint(dir, entries);

@@ -119,6 +119,7 @@ Yue2Model::~Yue2Model() {
   for (auto& e : row_events)
     if (e) cudaEventDestroy(e);
   pool.clear();
+  for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
   for (void* p : allocations) cudaFree(p);
   if (pinned_rows) cudaFreeHost(pinned_rows);
   if (pinned_flags) cudaFreeHost(pinned_flags);
@@ -162,7 +163,23 @@ extern "C" {
 
 const char* yue2_last_error(void) { return y2::g_error.c_str(); }
 
+static int create_model(int device, const Yue2Config* cfg, uint64_t tp_rank, uint64_t tp_world, Yue2Model** out);
+
 int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
+  return create_model(device, cfg, 0, 1, out);
+}
+
+int yue2_model_create_tp(int device, const Yue2Config* cfg, uint64_t tp_rank, uint64_t tp_world, Yue2Model** out) {
+  if (!cfg || !out) return fail(YUE2_ERR_INVALID, "null argument");
+  if (tp_world < 1 || tp_world > (uint64_t)kTpMaxWorld || tp_rank >= tp_world)
+    return fail(YUE2_ERR_INVALID, "tensor-parallel rank/world out of range (world at most 8)");
+  if (cfg->num_attention_heads % tp_world || cfg->num_key_value_heads % tp_world || cfg->intermediate_size % tp_world ||
+      (cfg->intermediate_size / tp_world) % 8 || cfg->vocab_size < tp_world)
+    return fail(YUE2_ERR_INVALID, "heads, KV heads and intermediate size must split evenly over the ranks");
+  return create_model(device, cfg, tp_rank, tp_world, out);
+}
+
+static int create_model(int device, const Yue2Config* cfg, uint64_t tp_rank, uint64_t tp_world, Yue2Model** out) {
   if (!cfg || !out) return fail(YUE2_ERR_INVALID, "null argument");
   *out = nullptr;
   const Yue2Config& c = *cfg;
@@ -189,8 +206,14 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   Yue2Model* m = new Yue2Model();
   m->device = device;
   m->cfg = c;
-  m->g = Geometry{(int)c.hidden_size, (int)c.num_attention_heads, (int)c.num_key_value_heads, (int)c.head_dim,
-                  (int)c.intermediate_size, (int)c.vocab_size, (int)c.num_hidden_layers, c.rms_norm_eps};
+  const uint64_t TP = tp_world;  // this rank's share of heads, KV heads, MLP rows and vocabulary
+  m->tp_rank = (int)tp_rank;
+  m->tp_world = (int)TP;
+  m->head_row0 = (int)(c.vocab_size * tp_rank / TP);
+  m->head_rows = (int)(c.vocab_size * (tp_rank + 1) / TP) - m->head_row0;
+  m->g = Geometry{(int)c.hidden_size, (int)(c.num_attention_heads / TP), (int)(c.num_key_value_heads / TP),
+                  (int)c.head_dim, (int)(c.intermediate_size / TP), (int)c.vocab_size, (int)c.num_hidden_layers,
+                  c.rms_norm_eps};
   int rc = y2_set_device(m);
   if (rc) {
     delete m;
@@ -204,32 +227,41 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   m->sms = prop.multiProcessorCount;
   m->pool.page_bytes = page_bytes(m->g);
   // ---- weight arena: one allocation, 256-byte aligned sub-buffers
-  const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size, D = c.head_dim;
-  const size_t qd = c.num_attention_heads * D, kd = c.num_key_value_heads * D;
+  const size_t H = c.hidden_size, V = c.vocab_size, D = c.head_dim;
+  const size_t I = m->g.inter, qd = (size_t)m->g.heads * D, kd = (size_t)m->g.kvh * D;  // this rank's share
+  const size_t r = tp_rank;
   auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
   size_t total = 0;
   std::vector<std::pair<std::string, TensorSlot>> plan;
-  auto add = [&](const std::string& name, size_t rows, size_t cols, bool norm) {
+  // rows x cols of the full [frows, fcols] tensor from (row0, col0)
+  auto add = [&](const std::string& name, size_t rows, size_t cols, bool norm, size_t frows = 0, size_t fcols = 0,
+                 size_t row0 = 0, size_t col0 = 0) {
     TensorSlot t;
     t.rows = rows;
     t.cols = cols;
     t.norm = norm;
     t.offset = total;
+    t.full_rows = frows ? frows : rows;
+    t.full_cols = fcols ? fcols : cols;
+    t.row0 = row0;
+    t.col0 = col0;
     total += al(rows * cols * (norm ? 4 : 2));
     plan.push_back({name, t});
   };
   add("model.embed_tokens.weight", V, H, false);
-  if (!c.tie_word_embeddings) add("lm_head.weight", V, H, false);
+  if (!c.tie_word_embeddings) add("lm_head.weight", m->head_rows, H, false, V, H, m->head_row0, 0);
   add("model.norm.weight", 1, H, true);
   for (uint64_t l = 0; l < c.num_hidden_layers; ++l) {
     const std::string p = "model.layers." + std::to_string(l) + ".";
-    add(p + "self_attn.q_proj.weight", qd, H, false);
-    add(p + "self_attn.k_proj.weight", kd, H, false);
-    add(p + "self_attn.v_proj.weight", kd, H, false);
-    add(p + "self_attn.o_proj.weight", H, qd, false);
-    add(p + "mlp.gate_proj.weight", I, H, false);
-    add(p + "mlp.up_proj.weight", I, H, false);
-    add(p + "mlp.down_proj.weight", H, I, false);
+    // column split (output rows) of q|k|v by heads and of gate|up; row split (input
+    // columns) of o and down
+    add(p + "self_attn.q_proj.weight", qd, H, false, qd * TP, H, r * qd, 0);
+    add(p + "self_attn.k_proj.weight", kd, H, false, kd * TP, H, r * kd, 0);
+    add(p + "self_attn.v_proj.weight", kd, H, false, kd * TP, H, r * kd, 0);
+    add(p + "self_attn.o_proj.weight", H, qd, false, H, qd * TP, 0, r * qd);
+    add(p + "mlp.gate_proj.weight", I, H, false, I * TP, H, r * I, 0);
+    add(p + "mlp.up_proj.weight", I, H, false, I * TP, H, r * I, 0);
+    add(p + "mlp.down_proj.weight", H, I, false, H, I * TP, 0, r * I);
     add(p + "input_layernorm.weight", 1, H, true);
     add(p + "self_attn.q_norm.weight", 1, D, true);
     add(p + "self_attn.k_norm.weight", 1, D, true);
@@ -244,7 +276,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
   for (auto& kv : plan) m->slots[kv.first] = kv.second;
   auto ptr = [&](const std::string& n) { return (void*)(m->arena + m->slots[n].offset); };
   m->embed = (uint16_t*)ptr("model.embed_tokens.weight");
-  m->lm_head = c.tie_word_embeddings ? m->embed : (uint16_t*)ptr("lm_head.weight");
+  m->lm_head = c.tie_word_embeddings ? m->embed + (size_t)m->head_row0 * H : (uint16_t*)ptr("lm_head.weight");
   m->final_norm = (float*)ptr("model.norm.weight");
   m->layers.resize(c.num_hidden_layers);
   for (uint64_t l = 0; l < c.num_hidden_layers; ++l) {
@@ -292,6 +324,7 @@ int yue2_model_create(int device, const Yue2Config* cfg, Yue2Model** out) {
 int yue2_model_enable_nar(Yue2Model* m, uint64_t latent_dim, uint64_t max_latent_frames, float timestep_shift) {
   if (!m) return fail(YUE2_ERR_INVALID, "null model");
   if (m->nar_arena) return fail(YUE2_ERR_INVALID, "NAR tensors already enabled");
+  if (m->tp_world > 1) return fail(YUE2_ERR_INVALID, "the NAR tensors are not available on a tensor-parallel model");
   // Config::read validation (src/model.rs:50-72)
   if (!latent_dim || latent_dim % 8 || latent_dim > 4096 || !max_latent_frames || !(timestep_shift > 0.f) ||
       !std::isfinite(timestep_shift))
@@ -427,9 +460,12 @@ int yue2_model_init_synthetic(Yue2Model* m, uint64_t seed, float stddev, float n
         if (i + 1 < v.size()) v[i + 1] = round_bf16(norm_mean + stddev * (float)(rad * sin(6.283185307179586 * u2)));
       }
       CK(cudaMemcpy(m->slot_addr(t), v.data(), v.size() * 4, cudaMemcpyHostToDevice));
-    } else {
+    } else if (t.rows == t.full_rows && t.cols == t.full_cols) {
       CK(launch_fill_normal_bf16(m->stream, (uint16_t*)m->slot_addr(t), t.rows * t.cols, tseed, 0.f,
                                  stddev));
+    } else {  // a tensor-parallel shard: the values of the full tensor at the shard's positions
+      CK(launch_fill_normal_shard(m->stream, (uint16_t*)m->slot_addr(t), t.rows, t.cols, t.full_cols, t.row0, t.col0,
+                                  tseed, stddev));
     }
     m->loaded.insert(kv.first);
   }
@@ -510,6 +546,16 @@ int yue2_model_finalize(Yue2Model* m) {
     if ((rc = m->alloc(&p, 256))) return rc;
     m->flags = (int32_t*)p;
     CK(cudaMemset(p, 0, 256));
+    if (m->tp_world > 1) {  // tensor-parallel exchange buffers (tp.cu)
+      if ((rc = m->alloc(&p, (size_t)kTpRows * H * 4))) return rc;
+      m->tp_part = (float*)p;
+      if ((rc = m->alloc(&p, tp_recv_bytes(g.hidden, g.vocab)))) return rc;
+      m->tp_recv = (char*)p;
+      CK(cudaMemset(p, 0, tp_recv_bytes(g.hidden, g.vocab)));
+      if ((rc = m->alloc(&p, 256))) return rc;
+      m->tp_epoch = (uint32_t*)p;
+      CK(cudaMemset(p, 0, 256));
+    }
     CK(cudaMallocHost(&m->pinned_rows, Yue2Model::kRowSlots * R * sizeof(DevRow)));
     CK(cudaMallocHost(&m->pinned_flags, 4096));
     m->workspace_ready = true;
@@ -574,7 +620,9 @@ int yue2_cache_fill_normal(Yue2Cache* c, uint64_t to, uint64_t seed) {
   if (to <= c->length) return 0;
   int rc = y2_set_device(c->m);
   if (rc) return rc;
-  CK(launch_kv_fill(c->m->stream, c->d_pages, c->m->g, (int)c->length, (int)to, seed));
+  const Yue2Model& m = *c->m;
+  CK(launch_kv_fill(m.stream, c->d_pages, m.g, (int)c->length, (int)to, seed, m.tp_rank * m.g.kvh,
+                    m.g.kvh * m.tp_world));
   CK(cudaStreamSynchronize(c->m->stream));
   c->length = to;
   return 0;
@@ -614,29 +662,45 @@ int splits_for(const Yue2Model& m, int R) {
   return std::max(1, std::min(m.max_splits, want));
 }
 
-// LM-head projection rows for a phase (model.rs:478-507): the window and the stop row.
+// LM-head projection rows for a phase (model.rs:478-507): the window and the stop row,
+// intersected with this rank's vocabulary rows [head_row0, head_row0 + head_rows) (all of
+// them without tensor parallelism). p.N = 0 when the rank holds none of them.
 static void head_params(const Yue2Model& m, int phase, GemvParams& p) {
   const size_t H = m.g.hidden;
   const int V = m.g.vocab;
-  p.wpair = nullptr;
+  int ranges[2][2];
+  int nr = 0;
   if (phase == kPhaseVocab) {
-    p.w[0] = p.w[1] = p.w[2] = m.lm_head;
-    p.seg_start[0] = 0;
-    p.seg_start[1] = p.seg_start[2] = V;
-    p.col0[0] = p.col0[1] = p.col0[2] = 0;
-    p.N = V;
-    return;
+    ranges[nr][0] = 0;
+    ranges[nr++][1] = V;
+  } else {
+    const int start = phase == kPhaseAbc ? 0 : (int)kCodecOffset;
+    const int end = phase == kPhaseAbc ? (int)kEOD : (int)(kCodecOffset + kCodecSize);
+    const int stop = phase == kPhaseAbc ? (int)kAbcEnd : (int)kMusicEnd;
+    ranges[nr][0] = start;
+    ranges[nr++][1] = end;
+    ranges[nr][0] = stop;
+    ranges[nr++][1] = stop + 1;
   }
-  const int start = phase == kPhaseAbc ? 0 : (int)kCodecOffset;
-  const int end = phase == kPhaseAbc ? (int)kEOD : (int)(kCodecOffset + kCodecSize);
-  const int stop = phase == kPhaseAbc ? (int)kAbcEnd : (int)kMusicEnd;
-  p.w[0] = m.lm_head + (size_t)start * H;
-  p.w[1] = p.w[2] = m.lm_head + (size_t)stop * H;
+  const int lo = m.head_row0, hi = m.head_row0 + m.head_rows;
+  p.wpair = nullptr;
+  int n = 0, seg = 0;
+  for (int i = 0; i < nr; ++i) {
+    const int a0 = std::max(ranges[i][0], lo), a1 = std::min(ranges[i][1], hi);
+    if (a1 <= a0) continue;
+    p.w[seg] = m.lm_head + (size_t)(a0 - lo) * H;
+    p.seg_start[seg] = n;
+    p.col0[seg] = a0;
+    n += a1 - a0;
+    ++seg;
+  }
+  for (int i = seg; i < 3; ++i) {
+    p.w[i] = seg ? p.w[seg - 1] : m.lm_head;
+    p.seg_start[i] = n;
+    p.col0[i] = seg ? p.col0[seg - 1] : 0;
+  }
   p.seg_start[0] = 0;
-  p.seg_start[1] = p.seg_start[2] = end - start;
-  p.col0[0] = start;
-  p.col0[1] = p.col0[2] = stop;
-  p.N = end - start + 1;
+  p.N = n;
 }
 
 int check_phase_vocab(const Yue2Model& m, int phase) {
@@ -674,7 +738,36 @@ cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float
   p.of = m.logits + (size_t)dst_row * V;
   p.ldo = V;
   p.skip = skip;
-  return launch_gemv(s, pdl, kXNorm, kEpiLogits, p, m.gemv_grid);
+  if (p.N > 0) {
+    cudaError_t e = launch_gemv(s, pdl, kXNorm, kEpiLogits, p, m.gemv_grid);
+    if (e != cudaSuccess) return e;
+  }
+  if (m.tp_world == 1) return cudaSuccess;
+  // every rank's vocabulary slice of the logits to every rank
+  TpParams tp = tp_params(m);
+  tp.R = R;
+  tp.n = V;
+  tp.col0 = m.head_row0;
+  tp.cols = m.head_rows;
+  tp.row_base = dst_row;
+  tp.site = 255;
+  return launch_tp_allgather(s, pdl, tp);
+}
+
+int tp_ready(const Yue2Model& m) {
+  if (m.tp_world > 1 && !m.tp_connected)
+    return fail(YUE2_ERR_INVALID, "tensor-parallel model: call yue2_tp_connect on every rank first");
+  return 0;
+}
+
+TpParams tp_params(const Yue2Model& m) {
+  TpParams p = {};
+  p.peers = m.tp_peers;
+  p.rank = m.tp_rank;
+  p.world = m.tp_world;
+  p.epoch = m.tp_epoch;
+  p.error = m.flags + 2;
+  return p;
 }
 
 // Parameters of layer l's kernels for R rows.
@@ -792,8 +885,10 @@ static LayerOps layer_ops(const Yue2Model& m, int l, int R, bool fused, const in
 cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int phase, const int32_t* skip) {
   const Geometry& g = m.g;
   const bool pdl = m.use_pdl;
-  cudaError_t e = launch_embed(s, pdl, m.rows, R, m.embed, g.hidden, g.vocab, m.x, m.flags + 0);
-  if (e != cudaSuccess) return e;
+  const bool tp = m.tp_world > 1;
+  cudaError_t e;
+  if (tp && (e = launch_tp_tick(s, pdl, m.tp_epoch)) != cudaSuccess) return e;
+  if ((e = launch_embed(s, pdl, m.rows, R, m.embed, g.hidden, g.vocab, m.x, m.flags + 0)) != cudaSuccess) return e;
   const int splits = splits_for(m, R);
   // Decode steps (head = true) give every row its own cache, so attention itself applies
   // the QK norm and RoPE and appends the row's K/V; prefill chunks (rows of one cache,
@@ -806,9 +901,28 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
     if ((e = launch_gemv(s, pdl, kXNorm, kEpiBf16, op.qkv, m.gemv_grid)) != cudaSuccess) return e;
     if (!fused && (e = launch_rope_append(s, pdl, op.rope, R)) != cudaSuccess) return e;
     if ((e = launch_attention(s, pdl, op.attn, R)) != cudaSuccess) return e;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.o, m.gemv_grid)) != cudaSuccess) return e;
+    if (!tp) {
+      if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.o, m.gemv_grid)) != cudaSuccess) return e;
+      if ((e = launch_gemv(s, pdl, kXNorm, kEpiSwiGLU, op.gu, m.gemv_grid)) != cudaSuccess) return e;
+      if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.down, m.gemv_grid)) != cudaSuccess) return e;
+      continue;
+    }
+    // tensor parallel: o and down leave f32 partial sums over this rank's input columns; the
+    // exchange adds every rank's in rank order and applies the residual
+    TpParams tpp = tp_params(m);
+    tpp.R = R;
+    tpp.n = g.hidden;
+    tpp.part = m.tp_part;
+    tpp.x = m.x;
+    GemvParams o = op.o, down = op.down;
+    o.of = down.of = m.tp_part;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiRawF32, o, m.gemv_grid)) != cudaSuccess) return e;
+    tpp.site = 2 * l;
+    if ((e = launch_tp_allreduce_residual(s, pdl, tpp)) != cudaSuccess) return e;
     if ((e = launch_gemv(s, pdl, kXNorm, kEpiSwiGLU, op.gu, m.gemv_grid)) != cudaSuccess) return e;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.down, m.gemv_grid)) != cudaSuccess) return e;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiRawF32, down, m.gemv_grid)) != cudaSuccess) return e;
+    tpp.site = 2 * l + 1;
+    if ((e = launch_tp_allreduce_residual(s, pdl, tpp)) != cudaSuccess) return e;
   }
   if (head && (e = encode_head(m, s, pdl, 0, R, 0, phase, skip)) != cudaSuccess) return e;
   return launch_step_end(s, pdl, m.rows, R);
@@ -817,7 +931,9 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
-  return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1;
+  const int tp = m.tp_world > 1;  // the tick, two exchanges per layer, the logits gather
+  return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1 +
+         tp * (1 + 2 * m.g.layers + (head ? 1 : 0));
 }
 
 // Runs (and caches as a CUDA graph) the forward step for R rows already in m.rows.
@@ -878,11 +994,15 @@ int take_flags(Yue2Model& m) {
 // device. When logits_row >= 0, the last id's final-normed hidden state goes through
 // the LM head into logits row `logits_row`.
 int prefill_device(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
-  if (m.use_prefill_gemm && n >= (uint64_t)kPrefillGemmMin) return prefill_gemm(m, c, d_ids, n, logits_row, phase);
+  // a tensor-parallel model runs prompts through the decode chain, kTpRows positions a pass
+  const bool tp = m.tp_world > 1;
+  if (!tp && m.use_prefill_gemm && n >= (uint64_t)kPrefillGemmMin)
+    return prefill_gemm(m, c, d_ids, n, logits_row, phase);
   const uint64_t L0 = c.length;
+  const uint64_t chunk = tp ? kTpRows : kMaxRows;
   int lastR = 0;
-  for (uint64_t start = 0; start < n; start += kMaxRows) {
-    const int R = (int)std::min<uint64_t>(kMaxRows, n - start);
+  for (uint64_t start = 0; start < n; start += chunk) {
+    const int R = (int)std::min<uint64_t>(chunk, n - start);
     std::vector<DevRow> rows(R);
     for (int r = 0; r < R; ++r) {
       rows[r] = DevRow{};
@@ -915,8 +1035,10 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
   if (!m || !caches || !ids) return fail(YUE2_ERR_INVALID, "null argument");
   if (!m->finalized) return fail(YUE2_ERR_INVALID, "model not finalized");
   if (rows < 1 || rows > (uint64_t)kMaxWideRows) return fail(YUE2_ERR_INVALID, "rows must be in [1, 256]");
+  if (m->tp_world > 1 && rows > (uint64_t)kTpRows)
+    return fail(YUE2_ERR_INVALID, "a tensor-parallel forward takes at most 2 rows");
   int rc = check_phase_vocab(*m, phase);
-  if (rc) return rc;
+  if (rc || (rc = tp_ready(*m))) return rc;
   std::set<const Yue2Cache*> seen;
   for (uint64_t r = 0; r < rows; ++r) {
     const Yue2Cache* c = caches[r];
@@ -937,7 +1059,7 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
     dr[r].advance = 1;
   }
   const float* out = m->logits;
-  if (rows >= (uint64_t)m->wide_min) {  // the GEMM path (gemm_rows.cu)
+  if (rows >= (uint64_t)m->wide_min && m->tp_world == 1) {  // the GEMM path (gemm_rows.cu)
     if ((rc = ensure_wide(*m))) return rc;
     CK(cudaMemcpyAsync(m->wide_rows, dr.data(), rows * sizeof(DevRow), cudaMemcpyHostToDevice, m->stream));
     if ((rc = encode_forward_wide(*m, m->stream, (int)rows, phase))) return rc;
@@ -961,7 +1083,7 @@ int yue2_prefill(Yue2Model* m, Yue2Cache* c, const int64_t* ids, uint64_t n, int
   if (c->length + n > c->capacity || c->length + n > (uint64_t)m->max_pos)
     return fail(YUE2_ERR_CAPACITY, "AR input exceeds cache/model context");
   int rc = check_phase_vocab(*m, phase);
-  if (rc) return rc;
+  if (rc || (rc = tp_ready(*m))) return rc;
   std::vector<int32_t> h(n);
   for (uint64_t i = 0; i < n; ++i) {
     if (ids[i] < 0 || ids[i] >= (int64_t)m->g.vocab) return fail(YUE2_ERR_TOKEN, "Token outside model vocabulary");

@@ -28,6 +28,9 @@ struct TensorSlot {
   size_t offset = 0, rows = 0, cols = 0;
   bool norm = false;      // f32 gain (or bias) vector; matrices are bf16
   char* base = nullptr;   // allocation holding the tensor (null: the model's weight arena)
+  // a tensor-parallel shard holds rows [row0, row0 + rows) and columns [col0, col0 + cols)
+  // of the full [full_rows, full_cols] tensor (the whole tensor without sharding)
+  size_t full_rows = 0, full_cols = 0, row0 = 0, col0 = 0;
 };
 
 int fail(int code, const std::string& msg);
@@ -97,6 +100,18 @@ struct Yue2Model {
   y2::DevRow* rows = nullptr;
   int32_t* flags = nullptr;  // [0] token out of range, [1] position outside RoPE table, [2] GEMV stream stall
   int max_splits = 64;
+
+  // ---- tensor parallelism (tp.cu): rank tp_rank of tp_world holds heads / tp_world query
+  // and key-value heads, intermediate / tp_world MLP rows, the matching input columns of o
+  // and down, and the LM-head rows [head_row0, head_row0 + head_rows) of the vocabulary
+  int tp_rank = 0, tp_world = 1;
+  int head_row0 = 0, head_rows = 0;
+  float* tp_part = nullptr;       // [kTpRows][hidden] f32 partial sums of o and down
+  char* tp_recv = nullptr;        // IPC-exported exchange words (tp.cu, tp_recv_bytes)
+  uint32_t* tp_epoch = nullptr;   // forwards run so far (the same count on every rank)
+  y2::TpPeers* tp_peers = nullptr;  // device copy of every rank's receive / logits addresses
+  std::vector<void*> tp_opened;   // peer mappings to close
+  bool tp_connected = false;
   static constexpr int kRowSlots = 32;  // pinned staging ring for row descriptors
   y2::DevRow* pinned_rows = nullptr;
   cudaEvent_t row_events[kRowSlots] = {};
@@ -144,6 +159,8 @@ cudaError_t encode_head(Yue2Model& m, cudaStream_t s, bool pdl, int x_row, int R
 cudaError_t encode_head_from(Yue2Model& m, cudaStream_t s, bool pdl, const float* x, int R, int dst_row, int phase,
                              const int32_t* skip);
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
+TpParams tp_params(const Yue2Model& m);  // the rank, peers, epoch and error flag of m's exchanges
+int tp_ready(const Yue2Model& m);        // 0, or an error when a TP model is not connected
 int attn_pipe_for(const Yue2Model& m, int R);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);

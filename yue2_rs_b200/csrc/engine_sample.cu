@@ -288,8 +288,11 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
   }
   if (R > kMaxWideRows)
     return fail(YUE2_ERR_INVALID, "at most 256 decode rows (CFG rows count twice) per session");
+  if (m->tp_world > 1 && R > kTpRows)
+    return fail(YUE2_ERR_INVALID, "a tensor-parallel session decodes one song (two rows with CFG)");
+  if ((rc = tp_ready(*m))) return rc;
   if ((rc = y2_set_device(m))) return rc;
-  const bool wide = R >= m->wide_min;  // the GEMM path (gemm_rows.cu), past 16 rows by default
+  const bool wide = R >= m->wide_min && m->tp_world == 1;  // the GEMM path (gemm_rows.cu)
   if (wide && (rc = ensure_wide(*m))) return rc;
   Yue2Session* ss = new Yue2Session();
   ss->m = m;

@@ -172,6 +172,34 @@ struct SampleParams {
   SampleAcc* acc;          // [nreq], {0, 0, ~0} between steps
 };
 
+// ---- tensor parallelism (tp.cu): the all-reduce and all-gather over peer memory
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpRows = 2;    // rows of a tensor-parallel pass (one song with CFG)
+constexpr int kTpCtas = 48;   // CTAs of a TP exchange kernel
+struct TpPeers {
+  uint2* recv[kTpMaxWorld];      // every rank's [2][kTpMaxWorld][kTpRows][hidden] exchange words
+  uint2* gather[kTpMaxWorld];    // every rank's [kMaxRows][vocab] logits words
+  float* logits[kTpMaxWorld];    // every rank's [kMaxRows][vocab] logits
+};
+struct TpParams {
+  const TpPeers* peers;
+  int rank, world, R;
+  const float* part;      // this rank's partial sums [R][n] (all-reduce) or nothing (all-gather)
+  float* x;               // residual [R][n] (all-reduce)
+  int n;                  // hidden (all-reduce) or vocab (all-gather)
+  int col0, cols;         // all-gather: this rank's logits columns
+  int row_base;           // all-gather: the first logits row (rows [row_base, row_base + R))
+  const uint32_t* epoch;  // forwards run so far
+  int site;               // exchange number within the forward
+  int32_t* error;         // set when a bounded wait gives up
+};
+cudaError_t launch_tp_allreduce_residual(cudaStream_t s, bool pdl, const TpParams& p);
+cudaError_t launch_tp_allgather(cudaStream_t s, bool pdl, const TpParams& p);
+cudaError_t launch_tp_tick(cudaStream_t s, bool pdl, uint32_t* epoch);
+size_t tp_recv_bytes(int hidden, int vocab);
+cudaError_t launch_fill_normal_shard(cudaStream_t s, uint16_t* dst, size_t rows, size_t cols, size_t full_cols,
+                                     size_t row0, size_t col0, uint64_t seed, float stddev);
+
 // launchers (return cudaError_t of the launch)
 cudaError_t launch_embed(cudaStream_t s, bool pdl, DevRow* rows, int R, const uint16_t* embed, int hidden,
                          int vocab, float* x, int32_t* error);
@@ -200,7 +228,7 @@ cudaError_t launch_fill_normal_bf16(cudaStream_t s, uint16_t* dst, size_t count,
                                     float stddev);
 cudaError_t launch_fill_f32(cudaStream_t s, float* dst, size_t count, float value);
 cudaError_t launch_kv_fill(cudaStream_t s, const uint64_t* pages, const Geometry& g, int from, int to,
-                           uint64_t seed);
+                           uint64_t seed, int head0, int full_kvh);
 
 cudaError_t prepare_kernels();  // configure every kernel for this device (call outside capture)
 size_t gemv_smem_bytes(int xmode, int K, int R);

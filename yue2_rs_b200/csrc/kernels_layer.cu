@@ -355,6 +355,7 @@ static cudaError_t launch_gemv_simt(cudaStream_t s, bool pdl, int xmode, int epi
       break;
     case kEpiRawF32:
       if (xmode == kXF32 && p.R == 1) return gemv_go<1, false, kXF32, kEpiRawF32>(s, pdl, p, grid);
+      if (xmode == kXBf16 && p.R <= 2) return gemv_rows<false, kXBf16, kEpiRawF32>(s, pdl, p, grid);
       break;
   }
   return cudaErrorInvalidValue;
@@ -552,14 +553,15 @@ cudaError_t prepare_kernels() {
   g_configure_only = true;
   cudaError_t e = cudaSuccess;
   const int pairs[][2] = {{kXNorm, kEpiBf16}, {kXBf16, kEpiResidual}, {kXNorm, kEpiSwiGLU},
-                          {kXNorm, kEpiLogits}, {kXBf16, kEpiLogits}, {kXF32, kEpiRawF32}};
+                          {kXNorm, kEpiLogits}, {kXBf16, kEpiLogits}, {kXF32, kEpiRawF32},
+                          {kXBf16, kEpiRawF32}};
   for (auto& pr : pairs)
     for (int K : {2048, 1536, 1024})
       for (int R : {1, 2, 4, 8}) {
         GemvParams p = {};
         p.K = K;
         p.N = 1;
-        p.R = pr[0] == kXF32 ? 1 : R;
+        p.R = pr[0] == kXF32 ? 1 : pr[1] == kEpiRawF32 ? std::min(R, 2) : R;
         if (e == cudaSuccess) e = launch_gemv(nullptr, false, pr[0], pr[1], p, 1);
       }
   for (int D : {64, 128, 256})
@@ -614,6 +616,23 @@ cudaError_t launch_fill_normal_bf16(cudaStream_t s, uint16_t* dst, size_t count,
   return cudaGetLastError();
 }
 
+// The rows x cols block at (row0, col0) of a full [*, full_cols] tensor filled as
+// fill_normal_kernel fills the whole tensor (a tensor-parallel shard of it).
+__global__ void fill_normal_shard_kernel(uint16_t* dst, size_t rows, size_t cols, size_t full_cols, size_t row0,
+                                         size_t col0, uint64_t seed, float stddev) {
+  const size_t count = rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t flat = (row0 + i / cols) * full_cols + col0 + i % cols;
+    dst[i] = f2bf_round(stddev * normal_at(seed, flat));
+  }
+}
+
+cudaError_t launch_fill_normal_shard(cudaStream_t s, uint16_t* dst, size_t rows, size_t cols, size_t full_cols,
+                                     size_t row0, size_t col0, uint64_t seed, float stddev) {
+  fill_normal_shard_kernel<<<1184, 256, 0, s>>>(dst, rows, cols, full_cols, row0, col0, seed, stddev);
+  return cudaGetLastError();
+}
+
 __global__ void fill_f32_kernel(float* dst, size_t count, float value) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
     dst[i] = value;
@@ -624,8 +643,11 @@ cudaError_t launch_fill_f32(cudaStream_t s, float* dst, size_t count, float valu
   return cudaGetLastError();
 }
 
-// Seeded N(0,1) bf16 keys/values for positions [from, to) of every layer.
-__global__ void kv_fill_kernel(const uint64_t* pages, Geometry g, int from, int to, uint64_t seed) {
+// Seeded N(0,1) bf16 keys/values for positions [from, to) of every layer. The values depend
+// on the KV head's index among all `full_kvh` heads (head0 + local head), so that a
+// tensor-parallel rank holds exactly its heads' share of the unsharded fill.
+__global__ void kv_fill_kernel(const uint64_t* pages, Geometry g, int from, int to, uint64_t seed, int head0,
+                               int full_kvh) {
   const size_t per_tok = (size_t)g.layers * 2 * g.kvh * g.dim;
   const size_t total = per_tok * (size_t)(to - from);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -638,16 +660,17 @@ __global__ void kv_fill_kernel(const uint64_t* pages, Geometry g, int from, int 
     const int kv = (int)(rem % 2);
     const int layer = (int)(rem / 2);
     uint16_t* page = reinterpret_cast<uint16_t*>(pages[tok >> kPageLog2]);
-    const uint64_t flat = (((uint64_t)layer * 2 + kv) * g.kvh + head) * 1048576ull * 64 + (uint64_t)tok * g.dim + d;
+    const uint64_t flat =
+        (((uint64_t)layer * 2 + kv) * full_kvh + head0 + head) * 1048576ull * 64 + (uint64_t)tok * g.dim + d;
     page[kv_offset(g, layer, kv, head) + (size_t)(tok & (kPageTokens - 1)) * g.dim + d] =
         f2bf_round(normal_at(seed, flat));
   }
 }
 
 cudaError_t launch_kv_fill(cudaStream_t s, const uint64_t* pages, const Geometry& g, int from, int to,
-                           uint64_t seed) {
+                           uint64_t seed, int head0, int full_kvh) {
   if (to <= from) return cudaSuccess;
-  kv_fill_kernel<<<1184, 256, 0, s>>>(pages, g, from, to, seed);
+  kv_fill_kernel<<<1184, 256, 0, s>>>(pages, g, from, to, seed, head0, full_kvh);
   return cudaGetLastError();
 }
 

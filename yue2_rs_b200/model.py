@@ -86,12 +86,19 @@ def _release_all():
 class Model:
     """A model resident on one GPU. Tensors are uploaded by their checkpoint names."""
 
-    def __init__(self, config, device=0):
+    def __init__(self, config, device=0, tp=None):
+        """tp = (rank, world): this process's shard of a tensor-parallel model
+        (yue2_model_create_tp); connect the ranks with yue2_rs_b200.tp.connect."""
         self.config = config.validate()
         self.device = device
+        self.tp = tp
         h = ctypes.c_void_p()
         c = config.to_c()
-        _lib.check(_lib.lib().yue2_model_create(device, ctypes.byref(c), ctypes.byref(h)))
+        if tp is None:
+            _lib.check(_lib.lib().yue2_model_create(device, ctypes.byref(c), ctypes.byref(h)))
+        else:
+            _lib.check(_lib.lib().yue2_model_create_tp(device, ctypes.byref(c), int(tp[0]), int(tp[1]),
+                                                       ctypes.byref(h)))
         self._h = h
         self._children = weakref.WeakSet()  # caches/generators to release before the model
         _LIVE.add(self)
@@ -116,10 +123,11 @@ class Model:
         return m
 
     @classmethod
-    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, device=0, nar=False):
+    def synthetic(cls, config, seed, std=0.02, norm_mean=0.0, device=0, nar=False, tp=None):
         """Seeded synthetic weights generated on the device: matrices N(0, std), RMSNorm
-        gains norm_mean + N(0, std), bf16. nar=True adds the flow-matching tensors."""
-        m = cls(config, device)
+        gains norm_mean + N(0, std), bf16. nar=True adds the flow-matching tensors. tp =
+        (rank, world): the shard of the same weights that rank holds."""
+        m = cls(config, device, tp=tp)
         if nar:
             m.enable_nar()
         _lib.check(_lib.lib().yue2_model_init_synthetic(m._h, seed, std, norm_mean))
@@ -254,7 +262,8 @@ class Cache:
 
     def read(self, layer, begin, count):
         c = self.model.config
-        w = c.num_key_value_heads * c.head_dim
+        world = self.model.tp[1] if self.model.tp else 1
+        w = c.num_key_value_heads // world * c.head_dim  # this rank's KV heads
         k = np.empty((count, w), dtype=np.uint16)
         v = np.empty((count, w), dtype=np.uint16)
         _lib.check(_lib.lib().yue2_cache_read(self._h, layer, begin, count, _ptr(k), _ptr(v)))
