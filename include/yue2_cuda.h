@@ -185,8 +185,9 @@ int yue2_model_load_checkpoint(Yue2Model* m, const char* dir, uint64_t* bytes_up
 /* Timing and parity hook for the prefill GEMMs: Y[C, N] = X[C, K] . W[N, K]^T on device
  * bf16 buffers (row-major, dense), `reps` timed runs after one untimed; impl 0 = cuBLASLt,
  * 1 = the tcgen05 kernel (K a multiple of 64), 2 = its gate|up form: W = [gate; up] of
- * [2N, K] and Y = bf16(bf16(silu(bf16 g)) * bf16 u) of [C, N] (N a multiple of 128).
- * `avg_ms` (nullable) gets the mean. */
+ * [2N, K] and Y = bf16(bf16(silu(bf16 g)) * bf16 u) of [C, N] (N a multiple of 128);
+ * 3 = the skinny tcgen05 kernel of the decode passes (C <= 256, K a multiple of 64),
+ * 4 = its gate|up form. `avg_ms` (nullable) gets the mean. */
 int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl, int reps,
                     double* avg_ms);
 /* Reserves device slots for the NAR (flow-matching) tensors of Model::open

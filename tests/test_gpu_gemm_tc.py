@@ -3,7 +3,11 @@ reference of the same bf16 operands and against cuBLASLt: Y = bf16(X . W^T) with
 accumulation, so every output lies within one bf16 rounding (plus f32 summation order) of
 the reference. Shapes cover one tile and one K block, partial row/column tiles, a K loop
 longer than the stage ring, and the prefill's q|k|v shape; the gate|up form with the
-SwiGLU epilogue is checked against the unfused GEMM put through the same roundings."""
+SwiGLU epilogue is checked against the unfused GEMM put through the same roundings. The
+skinny form (3..256 rows, the decode passes of several songs) is held to the same bounds
+over row counts on both sides of every padding step, ragged N, K loops that cut tiles
+between CTAs and a vocabulary-sized N where each CTA owns several whole tiles, and must
+repeat bit for bit."""
 import ctypes
 
 import pytest
@@ -23,7 +27,7 @@ def model():
 
 def _run(m, x, w, impl):
     C, K = x.shape
-    N = w.shape[0] // (2 if impl == 2 else 1)
+    N = w.shape[0] // (2 if impl in (2, 4) else 1)
     y = torch.full((C, N), float("nan"), dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()  # the library works on its own non-blocking stream
     ms = ctypes.c_double()
@@ -70,3 +74,39 @@ def test_tcgen05_gate_up_swiglu_epilogue(model):
     assert torch.isfinite(h.float()).all()
     assert ((h.float() - ref).abs() <= ref.abs() * 2.0 ** -7 + 1e-6).all()
     assert (h.float() == ref).float().mean() >= 0.99
+
+
+# ---- the skinny form (decode passes of 3..256 rows): weight rows on the MMA's M side,
+# (tile, K block) work split evenly over one CTA per SM, cut tiles summed in CTA order
+
+@pytest.mark.parametrize("C,N,K", [(3, 384, 256), (16, 5120, 3072), (17, 520, 320), (33, 3072, 3072),
+                                   (64, 3072, 8192), (100, 1000, 1024), (128, 16384, 3072), (256, 3072, 3072),
+                                   (48, 84000, 3072)])
+def test_skinny_gemm_matches_reference(model, C, N, K):
+    g = torch.Generator(device="cuda").manual_seed(C * 13 + N + K)
+    x = (torch.randn(C, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    ref = x.float() @ w.float().T
+    sk, _ = _run(model, x, w, 3)
+    assert torch.isfinite(sk.float()).all()
+    tol = ref.abs() * 2.0 ** -7 + 1e-3
+    assert ((sk.float() - ref).abs() <= tol).all()
+    assert (sk == ref.to(torch.bfloat16)).float().mean() >= 0.95
+    # the partial sums of cut tiles are added in a fixed order: the same bits every run
+    again, _ = _run(model, x, w, 3)
+    assert torch.equal(sk, again)
+
+
+@pytest.mark.parametrize("C,I,K", [(5, 384, 512), (32, 8192, 3072), (130, 1024, 3072), (256, 2816, 1024)])
+def test_skinny_gate_up_swiglu_epilogue(model, C, I, K):
+    g = torch.Generator(device="cuda").manual_seed(C + I)
+    x = (torch.randn(C, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    h, _ = _run(model, x, w, 4)
+    gu = (x.float() @ w.float().T).to(torch.bfloat16).float()
+    gt, ut = gu[:, :I], gu[:, I:]
+    ref = _bf(_bf(gt / (1.0 + torch.exp(-gt))) * ut)
+    assert torch.isfinite(h.float()).all()
+    # gate and up sums may round to the neighbouring bf16 value (f32 order): a few ulps
+    assert ((h.float() - ref).abs() <= ref.abs() * 2.0 ** -5 + 1e-3).all()
+    assert (h.float() == ref).float().mean() >= 0.95

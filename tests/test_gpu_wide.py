@@ -126,3 +126,21 @@ def test_generate_ten_songs_with_cfg_matches_replay(c1u_device, c1_prompt):
     want = _replay(c1u_device, reqs, s, Phase.VOCAB)
     for o, w in zip(outs, want):
         assert o.tokens == w and len(o.tokens) == 8
+
+
+def test_wide_rows_on_skinny_tcgen05_gemms():
+    """The oracle, GEMV-agreement and replay cases above with every GEMM of <= 256 rows on
+    the skinny tcgen05 kernel (YUE2_CUDA_SKINNY=1: q|k|v, o, gate|up with the SwiGLU
+    epilogue, down and the LM head). The switch is read when a model is created, so the
+    cases rerun in a child process."""
+    import os
+    import subprocess
+    import sys
+    if os.environ.get("YUE2_CUDA_SKINNY"):
+        pytest.skip("this process already runs with the switch set")
+    env = dict(os.environ, YUE2_CUDA_SKINNY="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", os.path.abspath(__file__),
+                        "-m", "gpu", "-k", "match_oracle or match_gemv_rows or matches_replay"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert "3 passed" in r.stdout, r.stdout[-2000:]

@@ -57,6 +57,8 @@ struct Yue2Model {
   int prefill_attn_tc5 = 0;
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
+  bool wide_pdl = true;          // passes of > 2 rows launch their kernels as programmatic dependents
+  bool gemm_skinny = false;      // GEMMs of <= 256 rows on the skinny tcgen05 kernel (YUE2_CUDA_SKINNY=1)
   bool gemm_tc = false;          // GEMMs of >= 128 rows on the tcgen05 kernel (YUE2_CUDA_GEMM=tc), else cuBLASLt
   y2::PrefillBufs* prefill = nullptr;
   // decode steps of more than kMaxRows rows (the GEMM path): row descriptors, logits
@@ -170,7 +172,7 @@ int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, i
 int ensure_wide(Yue2Model& m);
 int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase);
 int prepare_wide(Yue2Model& m, int R, int phase);
-int wide_kernels_per_step(const Yue2Model& m, int phase);
+int wide_kernels_per_step(const Yue2Model& m, int phase, int R);
 constexpr int kMaxWideRows = 256;    // rows of a wide decode step (128 songs with CFG)
 constexpr int kPrefillGemmMin = 3;   // shorter prompts go through the GEMV chain
 constexpr int kPrefillRows = 1024;   // capacity of the GEMM prefill buffers, in rows

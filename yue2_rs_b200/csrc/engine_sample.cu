@@ -471,7 +471,7 @@ void* yue2_session_stream(Yue2Session* ss) { return ss ? (void*)ss->m->stream : 
 
 uint64_t yue2_session_kernels_per_step(const Yue2Session* ss) {
   if (!ss) return 0;
-  const uint64_t forward = ss->wide ? (uint64_t)wide_kernels_per_step(*ss->m, ss->phase)
+  const uint64_t forward = ss->wide ? (uint64_t)wide_kernels_per_step(*ss->m, ss->phase, ss->R)
                                     : (uint64_t)kernels_per_step(*ss->m, true, ss->phase, ss->R);
   return forward + (ss->s.temperature != 0.f ? 1 : 0) + 2;
 }

@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(NT) residual_norm_kernel(float* __restrict__ x
                                                            const float* __restrict__ gamma, int H, float eps,
                                                            uint16_t* __restrict__ out) {
   __shared__ float red[NT / 32];
+  pdl_wait();  // x and y come from the preceding kernels
+  pdl_trigger();
   const int r = blockIdx.x, tid = threadIdx.x;
   float4* xr = reinterpret_cast<float4*>(x + (size_t)r * H);
   const uint2* yr = y ? reinterpret_cast<const uint2*>(y + (size_t)r * H) : nullptr;
@@ -106,6 +108,8 @@ __global__ void __launch_bounds__(NT) residual_norm_kernel(float* __restrict__ x
 // h = bf16(bf16(silu(g)) * u) over rows of gu = [g (I columns) | u (I columns)], all bf16
 // (the GEMV's SwiGLU epilogue on GEMM outputs). I % 8 == 0.
 __global__ void swiglu_kernel(const uint16_t* __restrict__ gu, int I, int C, uint16_t* __restrict__ h) {
+  pdl_wait();
+  pdl_trigger();
   const int I8 = I >> 3;
   const size_t total = (size_t)C * I8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -146,6 +150,7 @@ struct PrefillBufs {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   std::map<std::array<int, 6>, LtGemm> gemms;
+  SkinnyWork skinny;  // workspace and tickets of the skinny tcgen05 GEMM
 };
 
 void free_prefill(PrefillBufs* p) {
@@ -192,12 +197,18 @@ static int ensure_prefill(Yue2Model& m) {
   P->counters = (int32_t*)take((size_t)C * g.kvh * 4);
   P->ws_bytes = 32u << 20;
   P->ws = take(P->ws_bytes);
+  P->skinny.max_tiles = std::max(std::max(g.vocab, 2 * I), std::max(qd + 2 * kd, H)) / 128 + 2;
+  P->skinny.ws_bytes = gemm_skinny_ws_bytes(m.sms);
+  P->skinny.ws = (float*)take(P->skinny.ws_bytes);
+  P->skinny.tickets = (uint32_t*)take((size_t)gemm_skinny_tickets(P->skinny.max_tiles) * sizeof(uint32_t));
   // buffers taken before a failure stay with the model's allocations until it closes
   if (rc) {
     delete P;
     return rc;
   }
   cudaError_t e = cudaMemset(P->counters, 0, (size_t)C * g.kvh * 4);
+  if (e == cudaSuccess)
+    e = cudaMemset(P->skinny.tickets, 0, (size_t)gemm_skinny_tickets(P->skinny.max_tiles) * sizeof(uint32_t));
   if (e != cudaSuccess) {
     delete P;
     return cuda_fail(e, "prefill counters");
@@ -219,8 +230,17 @@ static int ensure_prefill(Yue2Model& m) {
 static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, void* Y, int ldy,
                    int C, bool f32out = false);
 
+static bool use_skinny(const Yue2Model& m, int C, int N, int K, int ldx, int ldy, const void* X, const void* W,
+                       const void* Y, bool swiglu) {
+  return m.gemm_skinny && C <= kSkinnyMaxRows && gemm_skinny_supported(C, N, K, ldx, ldy, X, W, Y, swiglu);
+}
+
 static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
                      int C) {
+  if (use_skinny(m, C, N, K, ldx, ldy, X, W, Y, false)) {
+    CK(launch_gemm_skinny(m.stream, m.wide_pdl, W, N, K, X, ldx, Y, ldy, C, false, m.prefill->skinny, m.flags + 2));
+    return 0;
+  }
   if (m.gemm_tc && C >= 128 && gemm_tc_supported(C, N, K, ldx, ldy, X, W, Y)) {
     CK(launch_gemm_tc(m.stream, W, N, K, X, ldx, Y, ldy, C, m.flags + 2));
     return 0;
@@ -322,10 +342,10 @@ static int gemm_concat(Yue2Model& m, const uint16_t* const* W, const int* N, int
   return 0;
 }
 
-static cudaError_t launch_residual_norm(cudaStream_t s, float* x, const uint16_t* y, const float* gamma, int H,
-                                        float eps, uint16_t* out, int C) {
+static cudaError_t launch_residual_norm(cudaStream_t s, bool pdl, float* x, const uint16_t* y, const float* gamma,
+                                        int H, float eps, uint16_t* out, int C) {
   void* args[] = {&x, &y, &gamma, &H, &eps, &out};
-  return launch_with(s, false, dim3(C), dim3(256), 0, (const void*)residual_norm_kernel<256>, args);
+  return launch_with(s, pdl, dim3(C), dim3(256), 0, (const void*)residual_norm_kernel<256>, args);
 }
 
 // Split-K decode attention with one query per row: decode rows (fused: QK norm, RoPE and
@@ -353,7 +373,44 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, DevRow* rows, int l, int 
   ap.max_pos = m.max_pos;
   ap.error = m.flags + 1;
   ap.pipe = fused ? 1 : 0;  // decode rows of the GEMM path: the pipelined tensor-core loop
-  CK(launch_attention(m.stream, false, ap, R));
+  CK(launch_attention(m.stream, m.wide_pdl, ap, R));
+  return 0;
+}
+
+// h = SwiGLU(gate . x, up . x) of R rows (P.xb -> P.h): one GEMM with the epilogue fused
+// (skinny tcgen05 for R <= 256, the prefill tcgen05 GEMM when opted in for R >= 128), else
+// the gate|up GEMM into P.gu and swiglu_kernel.
+static bool gate_up_fused(const Yue2Model& m, const PrefillBufs& P, const LayerW& w, int R) {
+  const Geometry& g = m.g;
+  const int H = g.hidden, I = g.inter;
+  if (w.up != w.gate + (size_t)I * H || I % 128) return false;
+  return use_skinny(m, R, I, H, H, I, P.xb, w.gate, P.h, true) ||
+         (m.gemm_tc && R >= 128 && gemm_tc_supported(R, I, H, H, I, P.xb, w.gate, P.h));
+}
+
+static int gate_up_swiglu(Yue2Model& m, PrefillBufs& P, const LayerW& w, int R) {
+  const Geometry& g = m.g;
+  const int H = g.hidden, I = g.inter;
+  cudaStream_t s = m.stream;
+  if (gate_up_fused(m, P, w, R)) {
+    if (use_skinny(m, R, I, H, H, I, P.xb, w.gate, P.h, true))
+      CK(launch_gemm_skinny(s, m.wide_pdl, w.gate, I, H, P.xb, H, P.h, I, R, true, m.prefill->skinny, m.flags + 2));
+    else
+      CK(launch_gemm_tc_swiglu(s, w.gate, I, H, P.xb, H, P.h, I, R, m.flags + 2));
+    return 0;
+  }
+  {
+    const uint16_t* W[2] = {w.gate, w.up};
+    const int N[2] = {I, I};
+    const int rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, R);
+    if (rc) return rc;
+  }
+  const uint16_t* gu = P.gu;
+  uint16_t* h = P.h;
+  int inter = I, nrows = R;
+  void* args[] = {&gu, &inter, &nrows, &h};
+  const int blocks = std::min(4 * m.sms, (int)(((size_t)R * (I / 8) + 255) / 256));
+  CK(launch_with(s, m.wide_pdl, dim3(blocks), dim3(256), 0, (const void*)swiglu_kernel, args));
   return 0;
 }
 
@@ -377,7 +434,7 @@ static int encode_layers(Yue2Model& m, PrefillBufs& P, const std::vector<LayerW>
   const int splits = std::max(1, std::min(std::min(m.max_splits, P.cap / R), 2 * m.sms / (g.kvh * R)));
   for (int l = 0; l < g.layers; ++l) {
     const LayerW& w = lw[l];
-    CK(launch_residual_norm(s, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, R));
+    CK(launch_residual_norm(s, m.wide_pdl, P.x, l ? P.y : nullptr, w.in_norm, H, g.eps, P.xb, R));
     {
       const uint16_t* W[3] = {w.q, w.k, w.v};
       const int N[3] = {qd, kd, kd};
@@ -422,24 +479,8 @@ static int encode_layers(Yue2Model& m, PrefillBufs& P, const std::vector<LayerW>
       }
     }
     if ((rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, R))) return rc;
-    CK(launch_residual_norm(s, P.x, P.y, w.post_norm, H, g.eps, P.xb, R));
-    if (m.gemm_tc && R >= 128 && w.up == w.gate + (size_t)I * H && I % 128 == 0 &&
-        gemm_tc_supported(R, I, H, H, I, P.xb, w.gate, P.h)) {
-      // gate|up GEMM with the SwiGLU epilogue fused (tcgen05)
-      CK(launch_gemm_tc_swiglu(s, w.gate, I, H, P.xb, H, P.h, I, R, m.flags + 2));
-    } else {
-      {
-        const uint16_t* W[2] = {w.gate, w.up};
-        const int N[2] = {I, I};
-        if ((rc = gemm_concat(m, W, N, 2, H, P.xb, H, P.gu, 2 * I, R))) return rc;
-      }
-      const uint16_t* gu = P.gu;
-      uint16_t* h = P.h;
-      int inter = I, nrows = R;
-      void* args[] = {&gu, &inter, &nrows, &h};
-      const int blocks = std::min(4 * m.sms, (int)(((size_t)R * (I / 8) + 255) / 256));
-      CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)swiglu_kernel, args));
-    }
+    CK(launch_residual_norm(s, m.wide_pdl, P.x, P.y, w.post_norm, H, g.eps, P.xb, R));
+    if ((rc = gate_up_swiglu(m, P, w, R))) return rc;
     if ((rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, R))) return rc;
   }
   return 0;
@@ -462,7 +503,7 @@ static int prefill_chunk(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint6
   const int rc = encode_layers(m, P, m.layers, P.rows, C, false, c.d_pages, (int)(L0 + start));
   if (rc) return rc;
   // the last layer's residual (the LM head applies the final norm itself)
-  CK(launch_residual_norm(s, P.x, P.y, nullptr, g.hidden, g.eps, nullptr, C));
+  CK(launch_residual_norm(s, m.wide_pdl, P.x, P.y, nullptr, g.hidden, g.eps, nullptr, C));
   return 0;
 }
 
@@ -490,6 +531,8 @@ static void head_span(const Yue2Model& m, int phase, int& lo, int& hi, int& star
 // (the rest of the row is already -inf outside the full-vocabulary phase).
 __global__ void head_scatter_kernel(const uint16_t* __restrict__ h, int ldh, int R, int lo, int n, int start, int end,
                                     int stop, float* __restrict__ logits, int V) {
+  pdl_wait();
+  pdl_trigger();
   const size_t total = (size_t)R * n;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / n), j = (int)(i - (size_t)r * n), id = lo + j;
@@ -531,7 +574,7 @@ int prepare_wide(Yue2Model& m, int R, int phase) {
   const int n = hi - lo, ldh = (n + 7) & ~7;
   if ((rc = gemm_concat(m, Wqkv, Nqkv, 3, H, P.xb, H, P.qkv, qd + 2 * kd, R)) ||
       (rc = gemm_bf16(m, w.o, H, qd, P.attn, qd, P.y, H, R)) ||
-      (rc = gemm_concat(m, Wgu, Ngu, 2, H, P.xb, H, P.gu, 2 * I, R)) ||
+      (rc = gemm_concat(m, Wgu, Ngu, 2, H, P.xb, H, P.gu, 2 * I, R)) || (rc = gate_up_swiglu(m, P, w, R)) ||
       (rc = gemm_bf16(m, w.down, H, I, P.h, I, P.y, H, R)) ||
       (rc = gemm_bf16(m, m.lm_head + (size_t)lo * H, n, H, P.xb, H, m.wide_head, ldh, R)))
     return rc;
@@ -548,9 +591,9 @@ int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase) {
   PrefillBufs& P = *m.prefill;
   const Geometry& g = m.g;
   const int H = g.hidden, V = g.vocab;
-  CK(launch_embed(s, false, m.wide_rows, R, m.embed, H, V, P.x, m.flags + 0));
+  CK(launch_embed(s, m.wide_pdl, m.wide_rows, R, m.embed, H, V, P.x, m.flags + 0));
   if ((rc = encode_layers(m, *m.prefill, m.layers, m.wide_rows, R, true, nullptr, 0))) return rc;
-  CK(launch_residual_norm(s, P.x, P.y, m.final_norm, H, g.eps, P.xb, R));
+  CK(launch_residual_norm(s, m.wide_pdl, P.x, P.y, m.final_norm, H, g.eps, P.xb, R));
   int lo, hi, start, end, stop;
   head_span(m, phase, lo, hi, start, end, stop);
   const int n = hi - lo, ldh = (n + 7) & ~7;
@@ -562,16 +605,20 @@ int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase) {
     int ld = ldh, rows = R, vocab = V;
     void* args[] = {&h, &ld, &rows, &lo, (void*)&n, &start, &end, &stop, &logits, &vocab};
     const int blocks = std::min(8 * m.sms, (int)(((size_t)R * n + 255) / 256));
-    CK(launch_with(s, false, dim3(blocks), dim3(256), 0, (const void*)head_scatter_kernel, args));
+    CK(launch_with(s, m.wide_pdl, dim3(blocks), dim3(256), 0, (const void*)head_scatter_kernel, args));
   }
-  CK(launch_step_end(s, false, m.wide_rows, R));
+  CK(launch_step_end(s, m.wide_pdl, m.wide_rows, R));
   return 0;
 }
 
-// Kernels of this library per wide step (the cuBLASLt GEMMs not counted): embed, per layer
-// two norms, attention and SwiGLU, the final norm, [the -inf fill], the head scatter and
-// step_end.
-int wide_kernels_per_step(const Yue2Model& m, int phase) { return 1 + 4 * m.g.layers + 1 + (phase != kPhaseVocab) + 2; }
+// Kernels of this library per wide step of R rows (cuBLASLt GEMMs not counted): embed, per
+// layer two norms and attention, then either the four skinny GEMMs (q|k|v, o, gate|up with
+// SwiGLU, down) or the SwiGLU kernel, the final norm, [the -inf fill], the LM head (skinny)
+// and the head scatter, and step_end.
+int wide_kernels_per_step(const Yue2Model& m, int phase, int R) {
+  const bool sk = m.gemm_skinny && R <= kSkinnyMaxRows;
+  return 1 + (3 + (sk ? 4 : 1)) * m.g.layers + 1 + (phase != kPhaseVocab) + (sk ? 1 : 0) + 2;
+}
 
 int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
   const Geometry& g = m.g;
@@ -731,7 +778,7 @@ static int velocity_rows(Yue2Model* m, Yue2Cache* c, NarBufs& B, const float* st
     CK(launch_with(s, false, dim3((N + 127) / 128), dim3(128), 0, (const void*)prefill_rows_kernel, args));
   }
   if ((rc = encode_layers(*m, P, m->nar_layers, P.rows, N, false, c->d_pages, (int)c->length, false))) return rc;
-  CK(launch_residual_norm(s, P.x, P.y, m->final_norm, H, g.eps, P.xb, N));
+  CK(launch_residual_norm(s, m->wide_pdl, P.x, P.y, m->final_norm, H, g.eps, P.xb, N));
   if ((rc = gemm_lt(*m, W.llm2vae, L, H, P.xb, H, B.yf, L, N, true))) return rc;
   CK(launch_bias_round(s, B.yf, W.llm2vae_b, N, L, 0, B.lat_out, nullptr, m->sms));
   CK(cudaMemcpyAsync(out, B.lat_out + L, rows * (size_t)L * 4, cudaMemcpyDeviceToHost, s));
@@ -778,14 +825,16 @@ extern "C" int yue2_velocity(Yue2Model* m, Yue2Cache* c, const float* state, uin
 extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void* Y, int C, int N, int K, int impl,
                                int reps, double* avg_ms) {
   using namespace y2;
-  if (!m || !X || !W || !Y || C < 1 || N < 1 || K < 1 || reps < 1 || impl < 0 || impl > 2)
+  if (!m || !X || !W || !Y || C < 1 || N < 1 || K < 1 || reps < 1 || impl < 0 || impl > 4)
     return fail(YUE2_ERR_INVALID, "bad GEMM benchmark arguments");
   int rc = y2_set_device(m);
   if (rc || (rc = ensure_prefill(*m))) return rc;
   const uint16_t *x = (const uint16_t*)X, *w = (const uint16_t*)W;
   uint16_t* y = (uint16_t*)Y;
-  if (impl >= 1 && (!gemm_tc_supported(C, N, K, K, N, X, W, Y) || (impl == 2 && N % 128)))
+  if ((impl == 1 || impl == 2) && (!gemm_tc_supported(C, N, K, K, N, X, W, Y) || (impl == 2 && N % 128)))
     return fail(YUE2_ERR_INVALID, "shape not supported by the tcgen05 GEMM");
+  if (impl >= 3 && !gemm_skinny_supported(C, N, K, K, N, X, W, Y, impl == 4))
+    return fail(YUE2_ERR_INVALID, "shape not supported by the skinny tcgen05 GEMM");
   cudaEvent_t a = nullptr, b = nullptr;
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
@@ -797,6 +846,10 @@ extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void*
     } else if (impl == 2) {
       const cudaError_t e = launch_gemm_tc_swiglu(m->stream, w, N, K, x, K, y, N, C, m->flags + 2);
       if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_tc_swiglu");
+    } else if (impl >= 3) {
+      const cudaError_t e =
+          launch_gemm_skinny(m->stream, false, w, N, K, x, K, y, N, C, impl == 4, m->prefill->skinny, m->flags + 2);
+      if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_skinny");
     } else {
       rc = gemm_lt(*m, w, N, K, x, K, y, N, C);
     }

@@ -53,21 +53,13 @@ using tc::mbar_try_wait;
 using tc::sdesc_sw128;
 using tc::smem_u32;
 using tc::tmem_ld32;
-Y2_DEV void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
+using tc::mbar_arrive_expect_tx;
 // Bounded wait for the phase of the given parity; false (and *error set) when it gave up.
 Y2_DEV bool mbar_wait(uint64_t* b, uint32_t parity, int32_t* error) {
   return tc::mbar_wait_bounded(b, parity, error, kSpin);
 }
 
-Y2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
+using tc::tma_load_2d;
 
 // Instruction descriptor: dense, D f32, A and B bf16, both K-major, N = BN, M = BM.
 template <int BN>
@@ -302,6 +294,10 @@ int tile_cost(int C, int N, int BN, int sms) {
 }
 
 }  // namespace
+
+bool make_tma_map_bf16(void* map, const void* base, int rows, int cols, int ld, int box_rows) {
+  return make_map(static_cast<CUtensorMap*>(map), base, rows, cols, ld, box_rows);
+}
 
 bool gemm_tc_supported(int C, int N, int K, int ldx, int ldy, const void* X, const void* W, const void* Y) {
   return C >= 1 && N >= 1 && K >= BK && K % BK == 0 && ldx % 8 == 0 && ldy % 8 == 0 && ldx >= K && ldy >= N &&
