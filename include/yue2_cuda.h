@@ -99,6 +99,32 @@ void yue2_cuda_release_cache(size_t cache);
 int yue2_cuda_ar_stack(const float* input, float* out, float* shadow, const Yue2GpuLayer* layers, size_t count,
                        size_t hidden, size_t heads, size_t kv, size_t dim, size_t intermediate, size_t prefix,
                        size_t capacity, size_t cache, float eps, const float* cos, const float* sin);
+/* yue2_metal_stack (tensor.rs:164-180, metal.m:429-538): `rows` new rows ([rows, hidden]
+ * f32) through `count` layers after `prefix` cached positions whose f32 K/V rows
+ * ([prefix, kv*dim], bf16-valued) each layer carries; every row attends to every key (the
+ * prefix and all new rows). cos/sin are the rows' RoPE tables ([rows, dim/2]). Products in
+ * f32, bf16 roundings where the reference's shaders round; `out` gets the final residual
+ * stream [rows, hidden]. The bf16 prefix blocks stay cached per (cache, layer, prefix) until
+ * yue2_cuda_release_cache(cache). */
+int yue2_cuda_stack(const float* input, float* out, const Yue2GpuLayer* layers, size_t count, size_t rows,
+                    size_t hidden, size_t heads, size_t kv, size_t dim, size_t intermediate, size_t prefix,
+                    size_t cache, float eps, const float* cos, const float* sin);
+/* yue2_metal_linear (tensor.rs:135-145, metal.m:216-237): c[m, n] = a[m, k] . W[n, k]^T in
+ * f32 with W the converted checkpoint matrix (bf16 widened exactly; F32/F16 kept, rounded
+ * to bf16 when `round`), cached by (mapping, raw, n, k, dtype, round). */
+int yue2_cuda_linear(const float* a, const uint8_t* weight, size_t mapping, int dtype, int round, float* c, size_t m,
+                     size_t n, size_t k);
+/* yue2_metal_gemm (tensor.rs:207-219, metal.m:164-181): c = a . op(b) + beta c in f32;
+ * op(b) = b^T of a row-major [n, k] b when transpose_b, else b of [k, n]; row strides lda,
+ * ldb, ldc. m or n of 0: nothing to do (returns 1). */
+int yue2_cuda_gemm(const float* a, const float* b, float* c, size_t m, size_t n, size_t k, int transpose_b,
+                   size_t lda, size_t ldb, size_t ldc, float beta);
+/* yue2_metal_attention (tensor.rs:194-206, metal.m:330-362): GQA attention of q [rows,
+ * heads*dim] over k/v [keys, kv*dim], all f32: scores in f32, softmax over the visible keys
+ * (all of them when causal < 0, else the first min(keys, causal + row + 1)), f32 P.V,
+ * output rounded to bf16 (attention.metal:29-70). */
+int yue2_cuda_attention(const float* q, const float* k, const float* v, float* out, size_t rows, size_t keys,
+                        size_t heads, size_t kv, size_t dim, int64_t causal, float scale);
 /* yue2_metal_cached_attention (tensor.rs:181-192, metal.m:686-706): single-query GQA
  * attention over k/v rows [0, keys) ([keys, kv*dim] f32, bf16-valued), output bf16-rounded. */
 int yue2_cuda_cached_attention(const float* q, const float* k, const float* v, float* out, size_t keys,

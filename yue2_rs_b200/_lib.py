@@ -84,6 +84,11 @@ _PROTOS = {
     "yue2_cuda_ar_stack": (c_int, [c_p, c_p, c_p, c_p, c_size, c_size, c_size, c_size, c_size, c_size, c_size,
                                    c_size, c_size, c_f, c_p, c_p]),
     "yue2_cuda_cached_attention": (c_int, [c_p, c_p, c_p, c_p, c_size, c_size, c_size, c_size, c_size, c_size]),
+    "yue2_cuda_stack": (c_int, [c_p, c_p, c_p, c_size, c_size, c_size, c_size, c_size, c_size, c_size, c_size,
+                                c_size, c_f, c_p, c_p]),
+    "yue2_cuda_linear": (c_int, [c_p, c_p, c_size, c_int, c_int, c_p, c_size, c_size, c_size]),
+    "yue2_cuda_gemm": (c_int, [c_p, c_p, c_p, c_size, c_size, c_size, c_int, c_size, c_size, c_size, c_f]),
+    "yue2_cuda_attention": (c_int, [c_p, c_p, c_p, c_p, c_size, c_size, c_size, c_size, c_size, ctypes.c_int64, c_f]),
     "yue2_attention_noalloc": (c_int, [c_p, c_p, c_p, c_p, c_u64, c_u64, c_u64, c_u64, c_p]),
     "yue2_model_create": (c_int, [c_int, ctypes.POINTER(Config), ctypes.POINTER(c_p)]),
     "yue2_model_create_tp": (c_int, [c_int, ctypes.POINTER(Config), c_u64, c_u64, ctypes.POINTER(c_p)]),

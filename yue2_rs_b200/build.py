@@ -18,7 +18,7 @@ OUT = os.path.join(HERE, "libyue2cuda.so")
 BUILD = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["kernels_layer.cu", "kernels_gemv.cu", "kernels_sample.cu", "gemm_rows.cu", "kernels_gemm_tc.cu", "kernels_gemm_skinny.cu", "kernels_prefill_attn.cu", "kernels_prefill_attn_tc.cu", "engine.cu", "engine_sample.cu", "checkpoint.cu", "dropin.cu", "noalloc.cu", "synthesize.cu", "tp.cu"]
+SOURCES = ["kernels_layer.cu", "kernels_gemv.cu", "kernels_sample.cu", "gemm_rows.cu", "kernels_gemm_tc.cu", "kernels_gemm_skinny.cu", "kernels_prefill_attn.cu", "kernels_prefill_attn_tc.cu", "engine.cu", "engine_sample.cu", "checkpoint.cu", "dropin.cu", "dropin_f32.cu", "noalloc.cu", "synthesize.cu", "tp.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off,-O2",
                 "-I" + CSRC, "-I" + INCLUDE]

@@ -22,6 +22,10 @@
 
 using namespace y2;
 
+// the f32 imports' context (dropin_f32.cu)
+void y2_f32_clear(bool release);
+void y2_f32_release_cache(size_t cache);
+
 namespace {
 
 // Gathers the f32 K and V rows of position `pos` of `count` single-layer contexts:
@@ -304,6 +308,7 @@ const char* yue2_cuda_name(void) {
 }
 
 void yue2_cuda_clear_weights(void) {
+  y2_f32_clear(false);
   DropIn& d = ctx();
   std::lock_guard<std::mutex> lock(d.mu);
   if (!d.init) return;
@@ -313,6 +318,7 @@ void yue2_cuda_clear_weights(void) {
 }
 
 void yue2_cuda_release_model(void) {
+  y2_f32_clear(true);
   DropIn& d = ctx();
   std::lock_guard<std::mutex> lock(d.mu);
   if (!d.init) return;
@@ -323,6 +329,7 @@ void yue2_cuda_release_model(void) {
 }
 
 void yue2_cuda_release_cache(size_t cache) {
+  y2_f32_release_cache(cache);
   DropIn& d = ctx();
   std::lock_guard<std::mutex> lock(d.mu);
   if (!d.init) return;

@@ -549,8 +549,6 @@ int yue2_model_finalize(Yue2Model* m) {
     m->flags = (int32_t*)p;
     CK(cudaMemset(p, 0, 256));
     if (m->tp_world > 1) {  // tensor-parallel exchange buffers (tp.cu)
-      if ((rc = m->alloc(&p, (size_t)kTpRows * H * 4))) return rc;
-      m->tp_part = (float*)p;
       if ((rc = m->alloc(&p, tp_recv_bytes(g.hidden, g.vocab)))) return rc;
       m->tp_recv = (char*)p;
       CK(cudaMemset(p, 0, tp_recv_bytes(g.hidden, g.vocab)));
@@ -909,22 +907,20 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
       if ((e = launch_gemv(s, pdl, kXBf16, kEpiResidual, op.down, m.gemv_grid)) != cudaSuccess) return e;
       continue;
     }
-    // tensor parallel: o and down leave f32 partial sums over this rank's input columns; the
-    // exchange adds every rank's in rank order and applies the residual
-    TpParams tpp = tp_params(m);
-    tpp.R = R;
-    tpp.n = g.hidden;
-    tpp.part = m.tp_part;
-    tpp.x = m.x;
+    // tensor parallel: o and down leave partial sums over this rank's input columns, which
+    // the same kernels exchange with every rank and add in rank order with the residual
     GemvParams o = op.o, down = op.down;
-    o.of = down.of = m.tp_part;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiRawF32, o, m.gemv_grid)) != cudaSuccess) return e;
-    tpp.site = 2 * l;
-    if ((e = launch_tp_allreduce_residual(s, pdl, tpp)) != cudaSuccess) return e;
+    for (GemvParams* p : {&o, &down}) {
+      p->tp_peers = m.tp_peers;
+      p->tp_epoch = m.tp_epoch;
+      p->tp_rank = m.tp_rank;
+      p->tp_world = m.tp_world;
+    }
+    o.tp_site = 2 * l;
+    down.tp_site = 2 * l + 1;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiTpReduce, o, m.gemv_grid)) != cudaSuccess) return e;
     if ((e = launch_gemv(s, pdl, kXNorm, kEpiSwiGLU, op.gu, m.gemv_grid)) != cudaSuccess) return e;
-    if ((e = launch_gemv(s, pdl, kXBf16, kEpiRawF32, down, m.gemv_grid)) != cudaSuccess) return e;
-    tpp.site = 2 * l + 1;
-    if ((e = launch_tp_allreduce_residual(s, pdl, tpp)) != cudaSuccess) return e;
+    if ((e = launch_gemv(s, pdl, kXBf16, kEpiTpReduce, down, m.gemv_grid)) != cudaSuccess) return e;
   }
   if (head && (e = encode_head(m, s, pdl, 0, R, 0, phase, skip)) != cudaSuccess) return e;
   return launch_step_end(s, pdl, m.rows, R);
@@ -933,9 +929,8 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
-  const int tp = m.tp_world > 1;  // the tick, two exchanges per layer, the logits gather
-  return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1 +
-         tp * (1 + 2 * m.g.layers + (head ? 1 : 0));
+  const int tp = m.tp_world > 1;  // the tick and the logits gather (o and down exchange in place)
+  return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1 + tp * (1 + (head ? 1 : 0));
 }
 
 // Runs (and caches as a CUDA graph) the forward step for R rows already in m.rows.

@@ -108,7 +108,6 @@ struct Yue2Model {
   // and down, and the LM-head rows [head_row0, head_row0 + head_rows) of the vocabulary
   int tp_rank = 0, tp_world = 1;
   int head_row0 = 0, head_rows = 0;
-  float* tp_part = nullptr;       // [kTpRows][hidden] f32 partial sums of o and down
   char* tp_recv = nullptr;        // IPC-exported exchange words (tp.cu, tp_recv_bytes)
   uint32_t* tp_epoch = nullptr;   // forwards run so far (the same count on every rank)
   y2::TpPeers* tp_peers = nullptr;  // device copy of every rank's receive / logits addresses

@@ -52,7 +52,11 @@ inline size_t page_bytes(const Geometry& g) { return (size_t)g.layers * 2 * g.kv
 
 // ---- GEMV (weight streaming; the SIMT kernel takes R <= 8, the tensor-core kernel R <= 16)
 enum XMode { kXBf16 = 0, kXNorm = 1, kXF32 = 2 };
-enum EpiMode { kEpiBf16 = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiLogits = 3, kEpiRawF32 = 4 };
+// kEpiTpReduce (tensor parallel, R <= 2): the o or down partial sums over this rank's input
+// columns go to every rank as exchange words, and x = bf16(x + bf16(sum over ranks)) is
+// formed in the same kernel (tp.cu describes the words).
+enum EpiMode { kEpiBf16 = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiLogits = 3, kEpiRawF32 = 4, kEpiTpReduce = 5 };
+struct TpPeers;
 
 struct GemvParams {
   const uint16_t* w[3];  // row segments; logical row n lives in segment s with seg_start[s] <= n
@@ -70,6 +74,11 @@ struct GemvParams {
   const int32_t* skip;   // optional: the whole launch is skipped when *skip != 0
   int32_t* error;        // optional: set to 1 when a bounded pipeline wait gives up
   int stages;            // set by the launcher: shared-memory ring depth of the streamed path
+  // kEpiTpReduce: the peers' exchange buffers, this rank, the forward counter and the
+  // exchange number (tags and parity halves as in tp.cu); `of` is the residual x [R, N]
+  const TpPeers* tp_peers;
+  const uint32_t* tp_epoch;
+  int tp_rank, tp_world, tp_site;
 };
 
 struct AttnParams {
@@ -175,25 +184,22 @@ struct SampleParams {
 // ---- tensor parallelism (tp.cu): the all-reduce and all-gather over peer memory
 constexpr int kTpMaxWorld = 8;
 constexpr int kTpRows = 2;    // rows of a tensor-parallel pass (one song with CFG)
-constexpr int kTpCtas = 48;   // CTAs of a TP exchange kernel
+constexpr int kTpCtas = 48;   // CTAs of the logits all-gather
 struct TpPeers {
-  uint2* recv[kTpMaxWorld];      // every rank's [2][kTpMaxWorld][kTpRows][hidden] exchange words
+  uint2* recv[kTpMaxWorld];      // every rank's [2][kTpMaxWorld][kTpRows][hidden] exchange words (o, down)
   uint2* gather[kTpMaxWorld];    // every rank's [kMaxRows][vocab] logits words
   float* logits[kTpMaxWorld];    // every rank's [kMaxRows][vocab] logits
 };
 struct TpParams {
   const TpPeers* peers;
   int rank, world, R;
-  const float* part;      // this rank's partial sums [R][n] (all-reduce) or nothing (all-gather)
-  float* x;               // residual [R][n] (all-reduce)
-  int n;                  // hidden (all-reduce) or vocab (all-gather)
-  int col0, cols;         // all-gather: this rank's logits columns
-  int row_base;           // all-gather: the first logits row (rows [row_base, row_base + R))
+  int n;                  // vocab
+  int col0, cols;         // this rank's logits columns
+  int row_base;           // the first logits row (rows [row_base, row_base + R))
   const uint32_t* epoch;  // forwards run so far
   int site;               // exchange number within the forward
   int32_t* error;         // set when a bounded wait gives up
 };
-cudaError_t launch_tp_allreduce_residual(cudaStream_t s, bool pdl, const TpParams& p);
 cudaError_t launch_tp_allgather(cudaStream_t s, bool pdl, const TpParams& p);
 cudaError_t launch_tp_tick(cudaStream_t s, bool pdl, uint32_t* epoch);
 size_t tp_recv_bytes(int hidden, int vocab);

@@ -14,6 +14,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "tp.cuh"
 
 namespace y2 {
 
@@ -274,6 +275,34 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
   cp_async_wait<0>();
   __syncthreads();
 
+  if (EPI == kEpiTpReduce) {  // tensor parallel: exchange, sum in rank order, residual
+    const TpPeers& P = *p.tp_peers;
+    const uint32_t tag = (*p.tp_epoch) * 256u + (uint32_t)p.tp_site + 1u;
+    const size_t half = (size_t)(p.tp_site & 1) * kTpMaxWorld * kTpRows * p.N;  // parity half (words)
+    const size_t slot = (size_t)kTpRows * p.N;                                   // one rank's words
+    for (int i = tid; i < nrows * RM; i += NT) {  // this CTA's partial sums to every rank
+      const int row_local = i / RM, r = i % RM;
+      if (r >= p.R) continue;
+      float sum = 0.f;
+      for (int b = 0; b < nb; ++b) sum += slots[(row_local * nb + b) * RM + r];
+      const size_t at = half + (size_t)p.tp_rank * slot + (size_t)r * p.N + row_begin + row_local;
+      for (int t = 0; t < p.tp_world; ++t) st_ll(P.recv[t] + at, sum, tag);
+    }
+    // every rank's sums of the same outputs (their CTA with this index computes the same rows)
+    bool ok = true;
+    const uint2* mine = P.recv[p.tp_rank] + half;
+    for (int i = tid; i < nrows * RM; i += NT) {
+      const int row_local = i / RM, r = i % RM;
+      if (r >= p.R) continue;
+      const int n = row_begin + row_local;
+      float s = 0.f;
+      for (int q = 0; q < p.tp_world; ++q) s += wait_ll(mine + (size_t)q * slot + (size_t)r * p.N + n, tag, p.error, ok);
+      float* xr = p.of + (size_t)r * p.ldo + n;
+      *xr = round_bf16(*xr + round_bf16(s));
+    }
+    return;
+  }
+
   // ---- epilogue: one thread per (row, activation row), rounding where Linear::finish does
   for (int i = tid; i < nrows * RM; i += NT) {
     const int row_local = i / RM, r = i % RM;
@@ -356,6 +385,11 @@ static cudaError_t launch_gemv_simt(cudaStream_t s, bool pdl, int xmode, int epi
     case kEpiRawF32:
       if (xmode == kXF32 && p.R == 1) return gemv_go<1, false, kXF32, kEpiRawF32>(s, pdl, p, grid);
       if (xmode == kXBf16 && p.R <= 2) return gemv_rows<false, kXBf16, kEpiRawF32>(s, pdl, p, grid);
+      break;
+    case kEpiTpReduce:
+      if (xmode == kXBf16 && p.R <= kTpRows &&
+          (g_configure_only || (p.tp_peers && p.tp_epoch && p.tp_world >= 1 && p.tp_world <= kTpMaxWorld)))
+        return gemv_rows<false, kXBf16, kEpiTpReduce>(s, pdl, p, grid);
       break;
   }
   return cudaErrorInvalidValue;
@@ -554,14 +588,14 @@ cudaError_t prepare_kernels() {
   cudaError_t e = cudaSuccess;
   const int pairs[][2] = {{kXNorm, kEpiBf16}, {kXBf16, kEpiResidual}, {kXNorm, kEpiSwiGLU},
                           {kXNorm, kEpiLogits}, {kXBf16, kEpiLogits}, {kXF32, kEpiRawF32},
-                          {kXBf16, kEpiRawF32}};
+                          {kXBf16, kEpiRawF32}, {kXBf16, kEpiTpReduce}};
   for (auto& pr : pairs)
     for (int K : {2048, 1536, 1024})
       for (int R : {1, 2, 4, 8}) {
         GemvParams p = {};
         p.K = K;
         p.N = 1;
-        p.R = pr[0] == kXF32 ? 1 : pr[1] == kEpiRawF32 ? std::min(R, 2) : R;
+        p.R = pr[0] == kXF32 ? 1 : (pr[1] == kEpiRawF32 || pr[1] == kEpiTpReduce) ? std::min(R, 2) : R;
         if (e == cudaSuccess) e = launch_gemv(nullptr, false, pr[0], pr[1], p, 1);
       }
   for (int D : {64, 128, 256})

@@ -2,19 +2,20 @@
 //
 // Rank r of W holds heads / W query heads and KV heads, intermediate / W MLP rows, the
 // matching input columns of o and down, and W-th of the LM-head vocabulary rows. A layer's
-// o and down projections then leave partial sums of the full hidden width on every rank;
-// `tp_allreduce_residual` adds them in rank order and applies the residual, which is the
-// reference's x = bf16(x + bf16(Wo . h)) (src/model.rs:586, src/tensor.rs:632-640) with
-// the f32 sum taken over the ranks' partial dot products. The LM head leaves each rank
-// its vocabulary slice; `tp_allgather` copies every slice to every rank, so each rank
-// holds identical logits and runs the same sampler on the same generator (no broadcast of
-// the sampled id is needed).
+// o and down projections then leave partial sums of the full hidden width on every rank.
+// The GEMV that computes them also exchanges them (its kEpiTpReduce epilogue,
+// kernels_layer.cu): every thread stores its outputs into every rank's receive buffer and
+// then adds all ranks' values of the same outputs in rank order with the residual, the
+// reference's x = bf16(x + bf16(Wo . h)) (src/model.rs:586, src/tensor.rs:632-640) with the
+// f32 sum taken over the ranks' partial dot products. The LM head leaves each rank its
+// vocabulary slice; `tp_allgather` copies every slice to every rank, so each rank holds
+// identical logits and runs the same sampler on the same generator (no broadcast of the
+// sampled id is needed).
 //
-// Both exchanges are one kernel each, without a library collective. Every thread stores its
-// elements of this rank's data into every rank's receive buffer (plain peer stores through
-// CUDA IPC mappings) as 8-byte words that pair the value with the exchange's tag, then reads
-// the words the other ranks stored for the same elements once they carry the tag: no flag,
-// no system-scope fence, one pass over NVLink. Tags only grow (the forward count times 256
+// No exchange uses a library collective. Values travel as 8-byte words that pair the
+// value with the exchange's tag (tp.cuh), stored into peers' buffers through CUDA IPC
+// mappings; a reader polls the words it needs until they carry the tag: no flag, no
+// system-scope fence, one pass over NVLink. Tags only grow (the forward count times 256
 // plus the exchange's number), so nothing needs resetting, and a rank is at most one
 // exchange ahead of another: the o/down buffers alternate by exchange parity. Every wait is
 // bounded (about a second of SM clocks); a wait that gives up sets the error flag, and the
@@ -29,6 +30,7 @@
 #include "common.cuh"
 #include "engine.h"
 #include "kernels.h"
+#include "tp.cuh"
 
 #define CK(expr)                                          \
   do {                                                    \
@@ -37,56 +39,6 @@
   } while (0)
 
 namespace y2 {
-
-constexpr long long kTpSpinCycles = 2000000000ll;
-
-// Low-latency exchange words: a value's bits with the exchange's tag in one aligned 64-bit
-// store (single-copy atomic), so a receiver polls the data itself and needs no flag or fence.
-Y2_DEV void st_ll(uint2* p, float v, uint32_t tag) {
-  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-Y2_DEV uint2 ld_ll(const uint2* p) {
-  unsigned long long w;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-  return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
-}
-// Waits (bounded) until the word carries `tag`; its value then.
-Y2_DEV float wait_ll(const uint2* p, uint32_t tag, int32_t* error, bool& ok) {
-  uint2 v = ld_ll(p);
-  if (v.y >= tag || !ok) return __uint_as_float(v.x);
-  const long long t0 = clock64();
-  while ((v = ld_ll(p)).y < tag)
-    if (clock64() - t0 > kTpSpinCycles) {
-      atomicExch(error, 1);
-      ok = false;
-      break;
-    }
-  return __uint_as_float(v.x);
-}
-
-// x[r][i] = bf16(x[r][i] + bf16(sum over ranks of part_q[r][i])), the sum in rank order.
-__global__ void __launch_bounds__(256) tp_allreduce_kernel(const TpParams p) {
-  pdl_wait();  // the partial sums come from the preceding GEMV
-  pdl_trigger();
-  const TpPeers& P = *p.peers;
-  const uint32_t tag = (*p.epoch) * 256u + (uint32_t)p.site + 1u;
-  const size_t half = (size_t)(p.site & 1) * kTpMaxWorld * kTpRows * p.n;  // parity half (words)
-  const int n = p.R * p.n;
-  const int stride = gridDim.x * blockDim.x;
-  const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
-  for (int i = i0; i < n; i += stride) {  // this rank's partials to every rank's slot `rank`
-    const float v = __ldcg(p.part + i);
-    for (int t = 0; t < p.world; ++t) st_ll(P.recv[t] + half + (size_t)p.rank * kTpRows * p.n + i, v, tag);
-  }
-  const uint2* mine = P.recv[p.rank] + half;
-  bool ok = true;
-  for (int i = i0; i < n; i += stride) {
-    float s = 0.f;
-    for (int q = 0; q < p.world; ++q) s += wait_ll(mine + (size_t)q * kTpRows * p.n + i, tag, p.error, ok);
-    p.x[i] = round_bf16(p.x[i] + round_bf16(s));
-  }
-}
 
 // Every rank's logits columns [col0_q, col0_q + cols_q) of rows [row_base, row_base + R) to
 // every rank: this rank's slice to the others' word buffers, then theirs into its logits.
@@ -122,13 +74,6 @@ __global__ void tp_tick_kernel(uint32_t* epoch) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x == 0) *epoch += 1;
-}
-
-cudaError_t launch_tp_allreduce_residual(cudaStream_t s, bool pdl, const TpParams& p) {
-  if (p.R < 1 || p.R > kTpRows || p.world < 1 || p.world > kTpMaxWorld) return cudaErrorInvalidValue;
-  TpParams copy = p;
-  void* args[] = {&copy};
-  return launch_with(s, pdl, dim3(kTpCtas), dim3(256), 0, (const void*)tp_allreduce_kernel, args);
 }
 
 cudaError_t launch_tp_allgather(cudaStream_t s, bool pdl, const TpParams& p) {
