@@ -658,6 +658,9 @@ namespace y2 {
 
 // Splits per (row, kv head): as many as fill one wave of attention CTAs (two per SM).
 int splits_for(const Yue2Model& m, int R) {
+  // 16 splits per (kv head, row) where that fills the GPU (measured: at least as fast as
+  // two CTAs per SM's worth, 2.046 against 2.066 ms/step at 4,096 positions)
+  if (R <= kMaxRows && m.g.kvh * R >= 8) return 16;
   const int want = (2 * m.sms) / (m.g.kvh * R);
   return std::max(1, std::min(m.max_splits, want));
 }
