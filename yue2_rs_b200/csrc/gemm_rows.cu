@@ -169,6 +169,8 @@ static int lt_fail(cublasStatus_t st, const char* what) {
   return fail(YUE2_ERR_CUDA, std::string(what) + " failed: cuBLASLt status " + std::to_string((int)st));
 }
 
+static int ensure_skinny(Yue2Model& m);
+
 static int ensure_prefill(Yue2Model& m) {
   if (m.prefill) return 0;
   const Geometry& g = m.g;
@@ -197,18 +199,14 @@ static int ensure_prefill(Yue2Model& m) {
   P->counters = (int32_t*)take((size_t)C * g.kvh * 4);
   P->ws_bytes = 32u << 20;
   P->ws = take(P->ws_bytes);
-  P->skinny.max_tiles = std::max(std::max(g.vocab, 2 * I), std::max(qd + 2 * kd, H)) / 128 + 2;
-  P->skinny.ws_bytes = gemm_skinny_ws_bytes(m.sms);
-  P->skinny.ws = (float*)take(P->skinny.ws_bytes);
-  P->skinny.tickets = (uint32_t*)take((size_t)gemm_skinny_tickets(P->skinny.max_tiles) * sizeof(uint32_t));
+
   // buffers taken before a failure stay with the model's allocations until it closes
   if (rc) {
     delete P;
     return rc;
   }
   cudaError_t e = cudaMemset(P->counters, 0, (size_t)C * g.kvh * 4);
-  if (e == cudaSuccess)
-    e = cudaMemset(P->skinny.tickets, 0, (size_t)gemm_skinny_tickets(P->skinny.max_tiles) * sizeof(uint32_t));
+
   if (e != cudaSuccess) {
     delete P;
     return cuda_fail(e, "prefill counters");
@@ -219,6 +217,25 @@ static int ensure_prefill(Yue2Model& m) {
     return lt_fail(st, "cublasLtCreate");
   }
   m.prefill = P;
+  return m.gemm_skinny ? ensure_skinny(m) : 0;
+}
+
+// The skinny GEMM's workspace and tickets (kernels_gemm_skinny.cu), once per model.
+static int ensure_skinny(Yue2Model& m) {
+  SkinnyWork& w = m.prefill->skinny;
+  if (w.ws) return 0;
+  const Geometry& g = m.g;
+  const int qd = g.heads * g.dim, kd = g.kvh * g.dim;
+  const int max_tiles = std::max(std::max(g.vocab, 2 * g.inter), std::max(qd + 2 * kd, g.hidden)) / 128 + 2;
+  const size_t tbytes = (size_t)gemm_skinny_tickets(max_tiles) * sizeof(uint32_t);
+  void *ws = nullptr, *tk = nullptr;
+  int rc = m.alloc(&ws, gemm_skinny_ws_bytes(m.sms));
+  if (rc || (rc = m.alloc(&tk, tbytes))) return rc;
+  CK(cudaMemset(tk, 0, tbytes));
+  w.max_tiles = max_tiles;
+  w.ws_bytes = gemm_skinny_ws_bytes(m.sms);
+  w.tickets = (uint32_t*)tk;
+  w.ws = (float*)ws;
   return 0;
 }
 
@@ -835,6 +852,7 @@ extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void*
     return fail(YUE2_ERR_INVALID, "shape not supported by the tcgen05 GEMM");
   if (impl >= 3 && !gemm_skinny_supported(C, N, K, K, N, X, W, Y, impl == 4))
     return fail(YUE2_ERR_INVALID, "shape not supported by the skinny tcgen05 GEMM");
+  if (impl >= 3 && (rc = ensure_skinny(*m))) return rc;
   cudaEvent_t a = nullptr, b = nullptr;
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
