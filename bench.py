@@ -564,7 +564,11 @@ def main():
                               "frames_per_s": world * 4096 / syn_s,
                               "what": "yue2_synthesize: prefill of 5,121 ids + 8 velocity calls of 4,098 rows"}}
 
-    # ---- end to end through the public C ABI with host buffers (prefill included)
+    # ---- end to end through the public C ABI with host buffers (prefill included). One
+    # untimed call first: the first generate of a process pays one-time costs (library
+    # algorithm selection for the prefill GEMM shapes, lazy kernel loading, allocator growth)
+    # that a serving process pays once, not per song.
+    generate_batch(model, [Request(cond, seed=rank + 5, negative=uncond, scale=SCALE)], c2_sampling(512), Phase.VOCAB)
     barrier()
     t0 = time.perf_counter()
     outs = generate_batch(model, [Request(cond, seed=rank + 7, negative=uncond, scale=SCALE)], c2_sampling(512),
@@ -600,7 +604,8 @@ def main():
         "e2e": {"value": e2e_tokens / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "prefill_seconds": outs[0].prefill_seconds, "library_seconds": outs[0].seconds,
                 "decode_ms": outs[0].decode_ms,
-                "what": "yue2_generate: 512 tokens per song incl. both 1,024-id prefills, host buffers in/out"},
+                "what": "yue2_generate: 512 tokens per song incl. both 1,024-id prefills, host buffers in/out; "
+                        "timed after one untimed call of the same shape"},
     }
     model.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
