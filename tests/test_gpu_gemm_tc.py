@@ -81,7 +81,7 @@ def test_tcgen05_gate_up_swiglu_epilogue(model):
 
 @pytest.mark.parametrize("C,N,K", [(3, 384, 256), (16, 5120, 3072), (17, 520, 320), (33, 3072, 3072),
                                    (64, 3072, 8192), (100, 1000, 1024), (128, 16384, 3072), (256, 3072, 3072),
-                                   (48, 84000, 3072)])
+                                   (48, 84000, 3072), (18, 1024, 2816), (18, 1536, 1024), (18, 1024, 1024)])
 def test_skinny_gemm_matches_reference(model, C, N, K):
     g = torch.Generator(device="cuda").manual_seed(C * 13 + N + K)
     x = (torch.randn(C, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
@@ -97,7 +97,8 @@ def test_skinny_gemm_matches_reference(model, C, N, K):
     assert torch.equal(sk, again)
 
 
-@pytest.mark.parametrize("C,I,K", [(5, 384, 512), (32, 8192, 3072), (130, 1024, 3072), (256, 2816, 1024)])
+@pytest.mark.parametrize("C,I,K", [(5, 384, 512), (32, 8192, 3072), (130, 1024, 3072), (256, 2816, 1024),
+                                   (18, 2816, 1024)])
 def test_skinny_gate_up_swiglu_epilogue(model, C, I, K):
     g = torch.Generator(device="cuda").manual_seed(C + I)
     x = (torch.randn(C, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)

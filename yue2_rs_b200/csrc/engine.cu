@@ -315,7 +315,10 @@ static int create_model(int device, const Yue2Config* cfg, uint64_t tp_rank, uin
     m->wide_min = std::max(2, std::min(kMaxRows + 1, env_int("YUE2_CUDA_WIDE_MIN", 3)));
     const char* gm = getenv("YUE2_CUDA_GEMM");
     m->gemm_tc = gm && std::string(gm) == "tc";
-    m->gemm_skinny = env_int("YUE2_CUDA_SKINNY", 0) != 0;
+    {
+      const int sk = env_int("YUE2_CUDA_SKINNY", -1);
+      m->skinny_rows = sk == 0 ? 0 : sk == 1 ? kSkinnyMaxRows : 16;
+    }
     m->wide_pdl = m->use_pdl && env_int("YUE2_CUDA_WIDE_PDL", 1) != 0;
   }
   *out = m;

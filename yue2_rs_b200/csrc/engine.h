@@ -58,7 +58,9 @@ struct Yue2Model {
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
   bool wide_pdl = true;          // passes of > 2 rows launch their kernels as programmatic dependents
-  bool gemm_skinny = false;      // GEMMs of <= 256 rows on the skinny tcgen05 kernel (YUE2_CUDA_SKINNY=1)
+  // passes of up to this many rows run their per-layer GEMMs on the skinny tcgen05 kernel
+  // (YUE2_CUDA_SKINNY: 0 off, 1 up to 256 rows; default 16, where it matches cuBLASLt)
+  int skinny_rows = 16;
   bool gemm_tc = false;          // GEMMs of >= 128 rows on the tcgen05 kernel (YUE2_CUDA_GEMM=tc), else cuBLASLt
   y2::PrefillBufs* prefill = nullptr;
   // decode steps of more than kMaxRows rows (the GEMM path): row descriptors, logits

@@ -150,7 +150,6 @@ struct PrefillBufs {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   std::map<std::array<int, 6>, LtGemm> gemms;
-  SkinnyWork skinny;  // workspace and tickets of the skinny tcgen05 GEMM
 };
 
 void free_prefill(PrefillBufs* p) {
@@ -168,8 +167,6 @@ void free_prefill(PrefillBufs* p) {
 static int lt_fail(cublasStatus_t st, const char* what) {
   return fail(YUE2_ERR_CUDA, std::string(what) + " failed: cuBLASLt status " + std::to_string((int)st));
 }
-
-static int ensure_skinny(Yue2Model& m);
 
 static int ensure_prefill(Yue2Model& m) {
   if (m.prefill) return 0;
@@ -217,27 +214,9 @@ static int ensure_prefill(Yue2Model& m) {
     return lt_fail(st, "cublasLtCreate");
   }
   m.prefill = P;
-  return m.gemm_skinny ? ensure_skinny(m) : 0;
-}
-
-// The skinny GEMM's workspace and tickets (kernels_gemm_skinny.cu), once per model.
-static int ensure_skinny(Yue2Model& m) {
-  SkinnyWork& w = m.prefill->skinny;
-  if (w.ws) return 0;
-  const Geometry& g = m.g;
-  const int qd = g.heads * g.dim, kd = g.kvh * g.dim;
-  const int max_tiles = std::max(std::max(g.vocab, 2 * g.inter), std::max(qd + 2 * kd, g.hidden)) / 128 + 2;
-  const size_t tbytes = (size_t)gemm_skinny_tickets(max_tiles) * sizeof(uint32_t);
-  void *ws = nullptr, *tk = nullptr;
-  int rc = m.alloc(&ws, gemm_skinny_ws_bytes(m.sms));
-  if (rc || (rc = m.alloc(&tk, tbytes))) return rc;
-  CK(cudaMemset(tk, 0, tbytes));
-  w.max_tiles = max_tiles;
-  w.ws_bytes = gemm_skinny_ws_bytes(m.sms);
-  w.tickets = (uint32_t*)tk;
-  w.ws = (float*)ws;
   return 0;
 }
+
 
 // Y[C, N] (row stride ldy) = X[C, K] (row stride ldx) . W[N, K]^T, bf16 in and out, f32
 // accumulation. Algorithms may split K only with an out-of-place f32 reduction in a
@@ -247,15 +226,18 @@ static int ensure_skinny(Yue2Model& m) {
 static int gemm_lt(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, void* Y, int ldy,
                    int C, bool f32out = false);
 
+// The skinny kernel for the per-layer matrices of passes of up to m.skinny_rows rows; the LM
+// head (more 128-row tiles than SMs, so several waves of CTAs each paying the kernel's
+// start) stays on cuBLASLt.
 static bool use_skinny(const Yue2Model& m, int C, int N, int K, int ldx, int ldy, const void* X, const void* W,
                        const void* Y, bool swiglu) {
-  return m.gemm_skinny && C <= kSkinnyMaxRows && gemm_skinny_supported(C, N, K, ldx, ldy, X, W, Y, swiglu);
+  return C <= m.skinny_rows && (N + 127) / 128 <= m.sms && gemm_skinny_supported(C, N, K, ldx, ldy, X, W, Y, swiglu);
 }
 
 static int gemm_bf16(Yue2Model& m, const uint16_t* W, int N, int K, const uint16_t* X, int ldx, uint16_t* Y, int ldy,
                      int C) {
   if (use_skinny(m, C, N, K, ldx, ldy, X, W, Y, false)) {
-    CK(launch_gemm_skinny(m.stream, m.wide_pdl, W, N, K, X, ldx, Y, ldy, C, false, m.prefill->skinny, m.flags + 2));
+    CK(launch_gemm_skinny(m.stream, m.wide_pdl, W, N, K, X, ldx, Y, ldy, C, false, m.flags + 2));
     return 0;
   }
   if (m.gemm_tc && C >= 128 && gemm_tc_supported(C, N, K, ldx, ldy, X, W, Y)) {
@@ -411,7 +393,7 @@ static int gate_up_swiglu(Yue2Model& m, PrefillBufs& P, const LayerW& w, int R) 
   cudaStream_t s = m.stream;
   if (gate_up_fused(m, P, w, R)) {
     if (use_skinny(m, R, I, H, H, I, P.xb, w.gate, P.h, true))
-      CK(launch_gemm_skinny(s, m.wide_pdl, w.gate, I, H, P.xb, H, P.h, I, R, true, m.prefill->skinny, m.flags + 2));
+      CK(launch_gemm_skinny(s, m.wide_pdl, w.gate, I, H, P.xb, H, P.h, I, R, true, m.flags + 2));
     else
       CK(launch_gemm_tc_swiglu(s, w.gate, I, H, P.xb, H, P.h, I, R, m.flags + 2));
     return 0;
@@ -630,11 +612,11 @@ int encode_forward_wide(Yue2Model& m, cudaStream_t s, int R, int phase) {
 
 // Kernels of this library per wide step of R rows (cuBLASLt GEMMs not counted): embed, per
 // layer two norms and attention, then either the four skinny GEMMs (q|k|v, o, gate|up with
-// SwiGLU, down) or the SwiGLU kernel, the final norm, [the -inf fill], the LM head (skinny)
-// and the head scatter, and step_end.
+// SwiGLU, down) or the SwiGLU kernel, the final norm, [the -inf fill], the head scatter and
+// step_end (the LM head GEMM is cuBLASLt's).
 int wide_kernels_per_step(const Yue2Model& m, int phase, int R) {
-  const bool sk = m.gemm_skinny && R <= kSkinnyMaxRows;
-  return 1 + (3 + (sk ? 4 : 1)) * m.g.layers + 1 + (phase != kPhaseVocab) + (sk ? 1 : 0) + 2;
+  const bool sk = R <= m.skinny_rows;
+  return 1 + (3 + (sk ? 4 : 1)) * m.g.layers + 1 + (phase != kPhaseVocab) + 2;
 }
 
 int prefill_gemm(Yue2Model& m, Yue2Cache& c, const int32_t* d_ids, uint64_t n, int logits_row, int phase) {
@@ -852,7 +834,6 @@ extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void*
     return fail(YUE2_ERR_INVALID, "shape not supported by the tcgen05 GEMM");
   if (impl >= 3 && !gemm_skinny_supported(C, N, K, K, N, X, W, Y, impl == 4))
     return fail(YUE2_ERR_INVALID, "shape not supported by the skinny tcgen05 GEMM");
-  if (impl >= 3 && (rc = ensure_skinny(*m))) return rc;
   cudaEvent_t a = nullptr, b = nullptr;
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
@@ -866,7 +847,7 @@ extern "C" int yue2_bench_gemm(Yue2Model* m, const void* X, const void* W, void*
       if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_tc_swiglu");
     } else if (impl >= 3) {
       const cudaError_t e =
-          launch_gemm_skinny(m->stream, false, w, N, K, x, K, y, N, C, impl == 4, m->prefill->skinny, m->flags + 2);
+          launch_gemm_skinny(m->stream, false, w, N, K, x, K, y, N, C, impl == 4, m->flags + 2);
       if (e != cudaSuccess) rc = cuda_fail(e, "launch_gemm_skinny");
     } else {
       rc = gemm_lt(*m, w, N, K, x, K, y, N, C);

@@ -230,22 +230,14 @@ bool make_tma_map_bf16(void* map, const void* base, int rows, int cols, int ld, 
 // Skinny tcgen05 GEMM for decode passes of 3..256 rows (kernels_gemm_skinny.cu):
 // Y[C, N] = bf16(X[C, K] . W[N, K]^T), or with `swiglu` (W = [gate; up], up at row N)
 // Y[C, N] = bf16(bf16(silu(bf16 g)) * bf16 u). The weight rows are the MMA's M side, the
-// activation rows its N side, and the (tile, K block) work is split evenly over one CTA per
-// SM; tiles shared by CTAs are summed in CTA order by the last to finish (deterministic).
-struct SkinnyWork {
-  float* ws = nullptr;          // partial accumulators: [ctas][2][acc cols][128] f32
-  uint32_t* tickets = nullptr;  // gemm_skinny_tickets(max_tiles) words, zero between launches
-  size_t ws_bytes = 0;
-  int max_tiles = 0;
-};
+// activation rows its N side; each tile's K range is split over the CTAs of one cluster,
+// which sum their partials in rank order through distributed shared memory.
 constexpr int kSkinnyMaxRows = 256;
 bool gemm_skinny_supported(int C, int N, int K, int ldx, int ldy, const void* X, const void* W, const void* Y,
                            bool swiglu);
-size_t gemm_skinny_ws_bytes(int sms);
-int gemm_skinny_tickets(int max_tiles);
 // pdl: launched as a programmatic dependent of the preceding kernel on the stream.
 cudaError_t launch_gemm_skinny(cudaStream_t s, bool pdl, const uint16_t* W, int N, int K, const uint16_t* X, int ldx,
-                               uint16_t* Y, int ldy, int C, bool swiglu, const SkinnyWork& work, int32_t* error);
+                               uint16_t* Y, int ldy, int C, bool swiglu, int32_t* error);
 
 cudaError_t launch_prefill_attention(cudaStream_t s, const PrefillAttnParams& p);
 // The same attention on tcgen05 (kernels_prefill_attn_tc.cu): head_dim 128.
