@@ -1,7 +1,8 @@
-"""Decode passes of more than 16 rows (many songs per GPU): the forward runs as tensor-core
-GEMMs over all rows (gemm_rows.cu) instead of the weight-streaming GEMV.
+"""Decode passes of three or more rows (several songs per GPU): the forward runs as
+tensor-core GEMMs over all rows (gemm_rows.cu) instead of the weight-streaming GEMV.
 
-  * logits against the oracle's decode path within the north_star tolerance;
+  * logits against the oracle's decode path within the north_star tolerance, at 18 rows
+    (cuBLASLt GEMMs) and 6 rows (the skinny tcgen05 GEMMs);
   * logits against the GEMV path on the same caches and ids (two passes of 10 rows);
   * the codec-window phase: window + stop row equal to the GEMV path's, -inf elsewhere;
   * generate_batch with 10 songs and CFG (20 rows) replays exactly against forward_rows
@@ -31,17 +32,18 @@ def _caches(model, prompts, extra, phase=Phase.VOCAB):
     return cs
 
 
-def test_wide_rows_match_oracle(c1_device, c1_oracle, c1_prompt):
-    prompts = _prompts(c1_prompt, 18)
+@pytest.mark.parametrize("rows", [18, 6])  # 6: the skinny tcgen05 GEMMs (default up to 16 rows)
+def test_wide_rows_match_oracle(c1_device, c1_oracle, c1_prompt, rows):
+    prompts = _prompts(c1_prompt, rows)
     teacher = c1_prompt[1]
     cs = _caches(c1_device, prompts, 3)
     ocs = [c1_oracle.cache(len(q) + 3) for q in prompts]
     for oc, q in zip(ocs, prompts):
         c1_oracle.prefill(q, oc, logits=False)
     for step in range(3):
-        ids = [teacher[(step * 18 + r) % len(teacher)] for r in range(18)]
+        ids = [teacher[(step * rows + r) % len(teacher)] for r in range(rows)]
         dev = c1_device.forward_rows(cs, ids)
-        for r in range(18):
+        for r in range(rows):
             ref = c1_oracle.forward([ids[r]], ocs[r])
             d = np.abs(dev[r].astype(np.float64) - ref)
             assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, (step, r, d.max(), d.mean())
@@ -143,4 +145,4 @@ def test_wide_rows_on_skinny_tcgen05_gemms():
                         "-m", "gpu", "-k", "match_oracle or match_gemv_rows or matches_replay"],
                        env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
-    assert "3 passed" in r.stdout, r.stdout[-2000:]
+    assert "4 passed" in r.stdout, r.stdout[-2000:]
