@@ -32,11 +32,14 @@ def config_3b_2layers():
 
 def pipelined_for(keys, rows, kvh):
     """The engine's choice of attention loop (attn_pipe_for_keys with splits_for): the
-    pipelined tile loop once a warp streams about 1.5 tiles of 32 keys. Splits: 16 where
-    kvh * rows >= 8, else two CTAs per SM's worth."""
+    pipelined tile loop once a warp streams about 1.5 tiles of 32 keys. Splits where
+    kvh * rows >= 8: 8 up to 8,192 positions, 16 beyond; else two CTAs per SM's worth."""
     import torch
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    splits = 16 if kvh * rows >= 8 else max(1, min(64, (2 * sms) // (kvh * rows)))
+    if kvh * rows >= 8:
+        splits = 8 if keys <= 8192 else 16
+    else:
+        splits = max(1, min(64, (2 * sms) // (kvh * rows)))
     return 2 * keys >= 3 * 32 * 4 * splits
 
 

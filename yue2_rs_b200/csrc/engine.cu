@@ -320,6 +320,7 @@ static int create_model(int device, const Yue2Config* cfg, uint64_t tp_rank, uin
       m->skinny_rows = sk == 0 ? 0 : sk == 1 ? kSkinnyMaxRows : 16;
     }
     m->wide_pdl = m->use_pdl && env_int("YUE2_CUDA_WIDE_PDL", 1) != 0;
+    m->attn_splits = std::max(0, env_int("YUE2_CUDA_ATTN_SPLITS", 0));
   }
   *out = m;
   return 0;
@@ -661,9 +662,12 @@ namespace y2 {
 
 // Splits per (row, kv head): as many as fill one wave of attention CTAs (two per SM).
 int splits_for(const Yue2Model& m, int R) {
-  // 16 splits per (kv head, row) where that fills the GPU (measured: at least as fast as
-  // two CTAs per SM's worth, 2.046 against 2.066 ms/step at 4,096 positions)
-  if (R <= kMaxRows && m.g.kvh * R >= 8) return 16;
+  if (m.attn_splits > 0) return std::min(m.max_splits, m.attn_splits);  // YUE2_CUDA_ATTN_SPLITS
+  // kv heads x rows >= 8 (the 3B CFG pair): 8 splits per (kv head, row) up to 8,192
+  // positions, 16 beyond (measured ms/step for the CFG pair, splits 8 / 12 / 16 / 24:
+  // 1k 2.003 / 2.013 / 2.012 / 2.017; 4k 2.021 / 2.048 / 2.041 / 2.419;
+  // 24k 2.962 / 2.804 / 2.790 / 3.117)
+  if (R <= kMaxRows && m.g.kvh * R >= 8) return m.ctx_hint <= 8192 ? 8 : 16;
   const int want = (2 * m.sms) / (m.g.kvh * R);
   return std::max(1, std::min(m.max_splits, want));
 }

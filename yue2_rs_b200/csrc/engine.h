@@ -57,6 +57,7 @@ struct Yue2Model {
   int prefill_attn_tc5 = 0;
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
+  int attn_splits = 0;             // > 0: decode attention splits per (kv head, row), forced
   bool wide_pdl = true;          // passes of > 2 rows launch their kernels as programmatic dependents
   // passes of up to this many rows run their per-layer GEMMs on the skinny tcgen05 kernel
   // (YUE2_CUDA_SKINNY: 0 off, 1 up to 256 rows; default 16, where it matches cuBLASLt)
