@@ -1,6 +1,7 @@
 // Decode attention and the QK norm + RoPE of one head, used by the decode attention kernels
 // (kernels_layer.cu) and the no-alloc entry point (noalloc.cu).
 #pragma once
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -507,6 +508,277 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
   }
   if (threadIdx.x == 0) a.counters[r * geo.kvh + g] = 0;
+}
+
+// ---- Cluster form for short decode contexts (fused decode rows, D <= 128). The CS CTAs of
+// one (kv head, row) form a thread-block cluster; CTA rank c owns the 32-key tiles
+// [c * TPC, min(ntiles, (c + 1) * TPC)), TPC = ceil(ntiles / CS), one per warp (warps loop
+// when TPC exceeds the warp count). Every tile is requested before griddepcontrol.wait,
+// the one holding the new position without that key: the CTA that computes the new K and V
+// (QK norm, RoPE) appends them to the cache and also writes them into its shared-memory
+// tile, so nothing in the launch reads them back from memory. Warps merge in shared memory,
+// then, after a cluster barrier, CTA c merges outputs [c * G * D / CS, ...) of the CS
+// partials through distributed shared memory, in rank order. No global partials, fence or
+// ticket; a second cluster barrier keeps the partials readable until every CTA is done.
+template <int D, int G>
+__host__ __device__ constexpr int attn_cluster_smem() {
+  return 2 * kClusterWarps * 32 * D * 2       // K and V tiles [NW][32][D] bf16
+         + G * D * 4                          // rotated q heads
+         + kClusterWarps * G * 32 * 4         // probabilities [NW][G][32]
+         + 2 * kClusterWarps * G * 4          // warp maxima and sums
+         + kClusterWarps * D * 4              // norm/rope scratch per warp
+         + 2 * D * 4                          // the new position's K and V
+         + G * (D + 2) * 4;                   // this CTA's partial (read by the cluster)
+}
+
+template <int D, int G>
+Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
+  static_assert(D <= 128 && G <= kClusterWarps, "cluster attention shape");
+  constexpr int NW = kClusterWarps, CPR = D / 8, DL = D / 32;
+  uint16_t* ktile = reinterpret_cast<uint16_t*>(smem_raw);  // [NW][32][D] (XOR-swizzled rows)
+  uint16_t* vtile = ktile + NW * 32 * D;                      // [NW][32][D]
+  float* qs = reinterpret_cast<float*>(vtile + NW * 32 * D);  // [G][D]
+  float* ps = qs + G * D;                                     // [NW][G][32]
+  float* wm = ps + NW * G * 32;                               // [NW][G]
+  float* wl = wm + NW * G;                                    // [NW][G]
+  float* wbuf_all = wl + NW * G;                              // [NW][D]
+  float* knew = wbuf_all + NW * D;                            // [D]
+  float* vnew = knew + D;                                     // [D]
+  float* cpart = vnew + D;                                    // [G][D + 2]: M, L, O[D]
+  float* wacc = reinterpret_cast<float*>(smem_raw);           // [NW][G][D] once the tiles are used
+
+  cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+  const int CS = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int g = blockIdx.y, r = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // every CTA of the cluster reads the same row: the returns below are taken by all of them
+  const DevRow row = a.rows[r];
+  if (!row.active) return;
+  const Geometry& geo = a.g;
+  const int pos = row.pos;
+  if (pos < 0 || pos >= a.max_pos) {
+    if (threadIdx.x == 0 && rank == 0) atomicExch(a.error, 1);
+    return;
+  }
+  const int keys = pos + 1, ntiles = (keys + 31) >> 5;
+  const int tpc = (ntiles + CS - 1) / CS;
+  const int t0 = rank * tpc, t1 = min(ntiles, t0 + tpc);
+  const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
+  uint16_t* kt = ktile + warp * 32 * D;
+  uint16_t* vt = vtile + warp * 32 * D;
+  auto stage = [&](int t) {  // the tile's keys below the new position (earlier steps wrote them)
+    const int key0 = t << 5;
+    const int nk = min(32, pos - key0);
+    const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
+    const uint16_t* kb = page + koff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    const uint16_t* vb = page + voff + (size_t)(key0 & (kPageTokens - 1)) * D;
+    for (int i = lane; i < 32 * CPR; i += 32) {
+      const int j = i / CPR, c = i % CPR;
+      if (j < nk) {
+        cp_async16(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
+        cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+      }
+    }
+    cp_async_commit();
+  };
+  if (t0 + warp < t1) stage(t0 + warp);
+
+  pdl_wait();
+  pdl_trigger();
+
+  const int width = (geo.heads + 2 * geo.kvh) * D;
+  const uint16_t* src = a.qkv + (size_t)r * width;
+  const float* ct = a.cos_tab + (size_t)pos * (D / 2);
+  const float* st = a.sin_tab + (size_t)pos * (D / 2);
+  float* wbuf = wbuf_all + warp * D;
+  for (int h = warp; h < G; h += NW) {
+    norm_rope_head<D>(src + (size_t)(g * G + h) * D, a.q_norm, geo.eps, ct, st, wbuf);
+    for (int i = lane; i < D; i += 32) qs[h * D + i] = wbuf[i];
+    __syncwarp();
+  }
+  if ((ntiles - 1) / tpc == rank) {  // this CTA's last tile holds `pos`: its K and V
+    const int kw = G + 2 <= NW ? G : 0;  // warps without a q head when there are two
+    uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
+    const size_t slot = (size_t)(pos & (kPageTokens - 1)) * D;
+    if (warp == kw) {
+      norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, a.k_norm, geo.eps, ct, st, wbuf);
+      uint16_t* dst = page + koff + slot;
+      for (int i = lane; i < D; i += 32) {
+        dst[i] = f2bf_exact(wbuf[i]);
+        knew[i] = wbuf[i];
+      }
+    } else if (warp == kw + 1) {
+      const uint16_t* vs = src + (size_t)(geo.heads + geo.kvh + g) * D;
+      uint16_t* dst = page + voff + slot;
+      for (int i = lane; i < D; i += 32) {
+        const uint16_t v = __ldcg(vs + i);
+        dst[i] = v;
+        vnew[i] = bf2f(v);
+      }
+    }
+  }
+  __syncthreads();
+
+  float m[G], l[G], acc[G][DL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
+  }
+  float* pw = ps + warp * G * 32;
+  for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
+    const int key0 = t << 5;
+    const int nk = min(32, keys - key0);
+    if (it > 0) stage(t);  // the warp's buffers are free again (end-of-iteration __syncwarp)
+    cp_async_wait<0>();
+    __syncwarp();
+    if (pos - key0 < 32) {  // the new position: its K and V from shared memory
+      const int j = pos - key0;
+      for (int c = lane; c < CPR; c += 32) {
+        uint32_t kw[4], vw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          kw[e] = pack_bf16x2(knew[c * 8 + 2 * e], knew[c * 8 + 2 * e + 1]);
+          vw[e] = pack_bf16x2(vnew[c * 8 + 2 * e], vnew[c * 8 + 2 * e + 1]);
+        }
+        *reinterpret_cast<uint4*>(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        *reinterpret_cast<uint4*>(vt + (size_t)j * D + c * 8) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      }
+      __syncwarp();
+    }
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.f;
+    if (lane < nk) {
+#pragma unroll 4
+      for (int c = 0; c < CPR; ++c) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(kt + (size_t)(lane * CPR + (c ^ (lane & 7))) * 8);
+        const float k0 = bf_lo(kv.x), k1 = bf_hi(kv.x), k2 = bf_lo(kv.y), k3 = bf_hi(kv.y);
+        const float k4 = bf_lo(kv.z), k5 = bf_hi(kv.z), k6 = bf_lo(kv.w), k7 = bf_hi(kv.w);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + h * D + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + h * D + c * 8 + 4);
+          float s = sc[h];
+          s = fmaf(qa.x, k0, s);
+          s = fmaf(qa.y, k1, s);
+          s = fmaf(qa.z, k2, s);
+          s = fmaf(qa.w, k3, s);
+          s = fmaf(qb.x, k4, s);
+          s = fmaf(qb.y, k5, s);
+          s = fmaf(qb.z, k6, s);
+          s = fmaf(qb.w, k7, s);
+          sc[h] = s;
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
+      const float mnew = fmaxf(m[h], warp_max(s));
+      const float alpha = m[h] == -INFINITY ? 0.f : __expf(m[h] - mnew);
+      const float pv = lane < nk ? __expf(s - mnew) : 0.f;
+      l[h] = l[h] * alpha + warp_sum(pv);
+      m[h] = mnew;
+      pw[h * 32 + lane] = pv;
+#pragma unroll
+      for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
+    }
+    __syncwarp();
+    for (int j = 0; j < nk; ++j) {
+      const uint16_t* vr = vt + (size_t)j * D + lane * DL;
+      float vv[DL];
+      if constexpr (DL == 2) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
+        vv[0] = bf_lo(w);
+        vv[1] = bf_hi(w);
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(vr);
+        vv[0] = bf_lo(w.x);
+        vv[1] = bf_hi(w.x);
+        vv[2] = bf_lo(w.y);
+        vv[3] = bf_hi(w.y);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float pj = pw[h * 32 + j];
+#pragma unroll
+        for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- this CTA's partial: warps merged in shared memory (tiles reused as accumulators)
+  __syncthreads();
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      wm[warp * G + h] = m[h];
+      wl[warp * G + h] = l[h];
+    }
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int e = 0; e < DL; ++e) wacc[((size_t)warp * G + h) * D + lane * DL + e] = acc[h][e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += NW * 32) {
+    const int h = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * G + h]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float mw = wm[w * G + h];
+      if (mw == -INFINITY) continue;
+      const float f = __expf(mw - M);
+      L = fmaf(wl[w * G + h], f, L);
+      O = fmaf(wacc[((size_t)w * G + h) * D + d], f, O);
+    }
+    float* ph = cpart + h * (D + 2);
+    if (d == 0) {
+      ph[0] = M;
+      ph[1] = L;
+    }
+    ph[2 + d] = O;
+  }
+  __syncwarp();
+  cl.sync();  // every CTA's partial is complete
+
+  // ---- outputs [rank * G * D / CS, ...) from every CTA's partial, in rank order
+  const float* parts[kClusterMax];
+#pragma unroll
+  for (int c = 0; c < kClusterMax; ++c) parts[c] = cl.map_shared_rank(cpart, c < CS ? c : 0);
+  const int n = G * D, i0 = rank * n / CS, i1 = (rank + 1) * n / CS;
+  const int outw = geo.heads * D;
+  for (int i = i0 + threadIdx.x; i < i1; i += NW * 32) {
+    const int h = i / D, d = i % D;
+    float mv[kClusterMax], lv[kClusterMax], ov[kClusterMax];
+#pragma unroll
+    for (int c = 0; c < kClusterMax; ++c)
+      if (c < CS) {
+        const float* pc = parts[c] + h * (D + 2);
+        mv[c] = pc[0];
+        lv[c] = pc[1];
+        ov[c] = pc[2 + d];
+      }
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kClusterMax; ++c)
+      if (c < CS) M = fmaxf(M, mv[c]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int c = 0; c < kClusterMax; ++c)
+      if (c < CS && mv[c] != -INFINITY) {
+        const float f = __expf(mv[c] - M);
+        L = fmaf(lv[c], f, L);
+        O = fmaf(ov[c], f, O);
+      }
+    a.out[(size_t)r * outw + (size_t)(g * G + h) * D + d] = f2bf_round(O / L);
+  }
+  __syncwarp();
+  cl.sync();  // the partials stay readable until every CTA of the cluster is done
 }
 
 }  // namespace y2

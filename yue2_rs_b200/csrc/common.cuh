@@ -130,17 +130,19 @@ Y2_DEV void stage_bf16_rows(const uint16_t* xb, int K, int R, unsigned char* xs,
 
 // Norm::apply (src/tensor.rs:1140-1157) of rows [0, R) of the f32 residual [R, K] with gains
 // gamma, as bf16 into shared memory rows of `pitch` bytes: s = bf16(1/sqrt(sum x^2 / K + eps)),
-// y = bf16(bf16(x * s) * gamma). K % 4 == 0. Up to four rows per pass: gains and the rows in
-// one round trip, one block reduction for all of them. `red` holds 64 floats. Every thread
-// of the block (NT threads, at most 8 warps for the one-pass form) takes part.
-template <int NT, bool CG = false>
+// y = bf16(bf16(x * s) * gamma). K % 4 == 0. Up to RP <= 4 rows per pass: gains and the
+// rows in one round trip, one block reduction for all of them (a caller that knows R <= RP
+// passes it, so that no registers hold rows that do not exist). `red` holds 64 floats.
+// Every thread of the block (NT threads, at most 8 warps for the one-pass form) takes part.
+template <int NT, bool CG = false, int RP = 4>
 Y2_DEV void stage_rmsnorm_rows(const float* xf, const float* gamma, int K, int R, float eps, unsigned char* xs,
                                size_t pitch, float* red) {
   auto ld = [](const float4* p) { return CG ? __ldcg(p) : *p; };
   static_assert(NT % 32 == 0 && NT <= 512, "block size");
   constexpr int NW = NT / 32;
   constexpr int kQ = 4;   // float4 columns per thread held in registers
-  constexpr int kRP = 4;  // rows per pass
+  static_assert(RP >= 1 && RP <= 4, "rows per pass");
+  constexpr int kRP = RP;  // rows per pass
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K4 = K >> 2;
   const float4* gm = reinterpret_cast<const float4*>(gamma);

@@ -321,6 +321,7 @@ static int create_model(int device, const Yue2Config* cfg, uint64_t tp_rank, uin
     }
     m->wide_pdl = m->use_pdl && env_int("YUE2_CUDA_WIDE_PDL", 1) != 0;
     m->attn_splits = std::max(0, env_int("YUE2_CUDA_ATTN_SPLITS", 0));
+    m->attn_cluster = std::max(-1, std::min(kClusterMax, env_int("YUE2_CUDA_ATTN_CLUSTER", -1)));
   }
   *out = m;
   return 0;
@@ -905,9 +906,11 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
   // consecutive positions) append all rows first with the separate kernel.
   const bool fused = head;
   const int pipe = attn_pipe_for(m, R);
+  const int cluster = fused ? attn_cluster_for(m, R) : 0;
   for (int l = 0; l < g.layers; ++l) {
     LayerOps op = layer_ops(m, l, R, fused, skip, splits);
     op.attn.pipe = pipe;
+    op.attn.cluster = cluster;
     if ((e = launch_gemv(s, pdl, kXNorm, kEpiBf16, op.qkv, m.gemv_grid)) != cudaSuccess) return e;
     if (!fused && (e = launch_rope_append(s, pdl, op.rope, R)) != cudaSuccess) return e;
     if ((e = launch_attention(s, pdl, op.attn, R)) != cudaSuccess) return e;
@@ -938,6 +941,26 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 
 int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
+// Up to kClusterKeys keys over the life of a captured forward (its context plus the positions
+// it will advance), decode passes of up to kMaxRows rows take the cluster form: one 32-key
+// tile per warp of 8-warp CTAs, ceil(tiles / 8) CTAs per (kv head, row), at most
+// kClusterCap (warps then take a second tile). Larger clusters wait for room in one GPC.
+// Measured decode step of the CFG pair (ms; split-K ticket kernel, then clusters of 3..8):
+//   1,040 positions: split 1.986, 3: 1.922, 4: 1.916, 5: 1.866, 6: 1.856
+//   1,500: split 1.935, 4: 1.840, 5: 1.850, 6: 1.813, 7 (auto, uncapped): 2.023
+//   1,900: split 1.903, 5: 1.876, 6: 1.857
+//   2,600: split 1.923, 5: 1.968, 8: 2.120
+constexpr int kClusterKeys = 2048;
+constexpr int kClusterCap = 6;
+int attn_cluster_for(const Yue2Model& m, int R) {
+  if (m.attn_cluster == 0 || m.g.dim > 128 || R > kMaxRows || m.attn_splits > 0) return 0;
+  if (m.attn_cluster > 0) return m.attn_cluster;
+  const int keys = m.ctx_hint + m.ctx_growth;
+  if (keys > kClusterKeys) return 0;
+  const int tiles = (keys + 31) / 32;
+  return std::max(1, std::min(kClusterCap, (tiles + kClusterWarps - 1) / kClusterWarps));
+}
+
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
   const int tp = m.tp_world > 1;  // the tick and the logits gather (o and down exchange in place)
   return 1 + (head ? 5 : 6) * m.g.layers + (head ? 1 + (phase != kPhaseVocab) : 0) + 1 + tp * (1 + (head ? 1 : 0));
@@ -945,7 +968,7 @@ int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
 
 // Runs (and caches as a CUDA graph) the forward step for R rows already in m.rows.
 int run_forward(Yue2Model& m, int R, bool head, int phase) {
-  const int key = R * 16 + (head ? 8 : 0) + phase + attn_pipe_for(m, R) * 4096;
+  const int key = R * 16 + (head ? 8 : 0) + phase + (attn_pipe_for(m, R) + 2 * attn_cluster_for(m, R)) * 8192;
   if (!m.use_graphs) {
     CK(encode_forward(m, m.stream, R, head, phase, nullptr));
     return 0;

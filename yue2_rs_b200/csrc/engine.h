@@ -58,6 +58,11 @@ struct Yue2Model {
   bool gemm_split_k = false;     // GEMMs may split K with an f32 out-of-place reduction (YUE2_CUDA_GEMM_SPLITK=1)
   int wide_min = 3;              // decode passes of at least this many rows use the GEMM path (YUE2_CUDA_WIDE_MIN)
   int attn_splits = 0;             // > 0: decode attention splits per (kv head, row), forced
+  // decode attention as CTA clusters merged in distributed shared memory while a captured
+  // forward's rows stay within kClusterKeys keys (YUE2_CUDA_ATTN_CLUSTER: -1 auto, 0 off,
+  // 1..8 CTAs per (kv head, row) forced); ctx_growth = positions a captured graph advances
+  int attn_cluster = -1;
+  int ctx_growth = 0;
   bool wide_pdl = true;          // passes of > 2 rows launch their kernels as programmatic dependents
   // passes of up to this many rows run their per-layer GEMMs on the skinny tcgen05 kernel
   // (YUE2_CUDA_SKINNY: 0 off, 1 up to 256 rows; default 16, where it matches cuBLASLt)
@@ -166,6 +171,8 @@ int kernels_per_step(const Yue2Model& m, bool head, int phase, int R);
 TpParams tp_params(const Yue2Model& m);  // the rank, peers, epoch and error flag of m's exchanges
 int tp_ready(const Yue2Model& m);        // 0, or an error when a TP model is not connected
 int attn_pipe_for(const Yue2Model& m, int R);
+// CTAs per (kv head, row) of the cluster form of decode attention, 0 for the split-K kernels
+int attn_cluster_for(const Yue2Model& m, int R);
 int run_forward(Yue2Model& m, int R, bool head, int phase);
 int upload_rows(Yue2Model& m, const std::vector<DevRow>& rows);
 int take_flags(Yue2Model& m);

@@ -426,6 +426,8 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
     if (wide && (rc = prepare_wide(*m, R, phase))) return bail(rc);
     m->ctx_hint = 0;
     for (int r = 0; r < R; ++r) m->ctx_hint = std::max(m->ctx_hint, (int)rows[r].pos + 1);
+    // the graph is replayed for every later token: the attention form must suit the whole run
+    m->ctx_growth = (int)std::min<uint64_t>(s->max_tokens, 1u << 20);
     cudaGraph_t graph;
     if ((e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
       return bail(cuda_fail(e, "capture"));
@@ -447,6 +449,7 @@ int yue2_session_create(Yue2Model* m, const Yue2Sampling* s, int phase, const Yu
     if (ce == cudaSuccess && draw) ce = cudaStreamWaitEvent(m->stream, m->ev_join, 0);
     if (ce == cudaSuccess) ce = launch_sample(m->stream, false, ss->sp, (int)n);
     e = cudaStreamEndCapture(m->stream, &graph);
+    m->ctx_growth = 0;
     if (wrc) {
       if (e == cudaSuccess) cudaGraphDestroy(graph);
       return bail(wrc);

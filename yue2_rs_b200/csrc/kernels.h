@@ -23,6 +23,8 @@ enum Phase { kPhaseAbc = 0, kPhaseSemantic = 1, kPhaseVocab = 2 };
 constexpr int kMaxRows = 16;       // rows per decode step / prefill chunk (8 songs with CFG)
 constexpr int kPageTokens = 64;    // KV page: 64 positions of every layer
 constexpr int kPageLog2 = 6;
+constexpr int kClusterWarps = 8;   // warps per CTA of the cluster form of decode attention
+constexpr int kClusterMax = 8;     // CTAs per (kv head, row) cluster, at most (portable size)
 
 struct DevRow {
   const uint64_t* pages;  // device array: base address of each page of this row's cache
@@ -98,6 +100,9 @@ struct AttnParams {
   int max_pos;
   int32_t* error;
   int pipe;  // 1: the pipelined tile loop (long contexts); passes of > kMaxRows rows always use it
+  // > 0 (fused decode rows, dim <= 128): that many CTAs per (kv head, row) as one thread-block
+  // cluster that merges its partials through distributed shared memory (short contexts)
+  int cluster;
 };
 
 // The pipelined attention loop pays off once a warp streams about 1.5 tiles of 32 keys or

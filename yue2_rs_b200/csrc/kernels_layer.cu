@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     for (int i = tid; i < (RM - p.R) * K8; i += NT) xz[i] = make_uint4(0, 0, 0, 0);
     if (XM == kXBf16) stage_bf16_rows<NT>(p.xb, K, p.R, xbase, (size_t)K * 2);
     else  // kXNorm: RMSNorm of the f32 residual (Norm::apply)
-      stage_rmsnorm_rows<NT>(p.xf, p.gamma, K, p.R, p.eps, xbase, (size_t)K * 2, red);
+      stage_rmsnorm_rows<NT, false, (RM < 4 ? RM : 4)>(p.xf, p.gamma, K, p.R, p.eps, xbase, (size_t)K * 2, red);
   }
   const int nrows = row_end - row_begin;
   for (int i = tid; i < nrows * nb * NP * RM; i += NT) slots[i] = 0.f;
@@ -561,14 +561,57 @@ static cudaError_t attn_go(cudaStream_t s, bool pdl, const AttnParams& p, int R)
   return launch_with(s, pdl, dim3(p.splits, p.g.kvh, R), dim3(128), smem, fn, args);
 }
 
+template <int D, int G>
+__global__ void __launch_bounds__(32 * kClusterWarps, 1) attn_cluster_kernel(const AttnParams a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  attn_cluster_item<D, G>(a, smem_raw);
+}
+
+template <int D, int G>
+static cudaError_t attn_cluster_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
+  const void* fn = (const void*)attn_cluster_kernel<D, G>;
+  constexpr int smem = attn_cluster_smem<D, G>();
+  cudaError_t e = ensure_smem_attr(fn, smem);
+  if (e != cudaSuccess || g_configure_only) return e;
+  if (!p.fused || p.cluster < 1 || p.cluster > kClusterMax) return cudaErrorInvalidValue;
+  AttnParams copy = p;
+  void* args[] = {&copy};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.cluster, p.g.kvh, R);
+  cfg.blockDim = dim3(32 * kClusterWarps);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // the CTAs of one (kv head, row)
+  attr[0].val.clusterDim.x = (unsigned)p.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+template <int D, int G>
+static cudaError_t attn_dim_go(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
+  if constexpr (D <= 128) {
+    if (p.cluster > 0 || g_configure_only) {
+      cudaError_t e = attn_cluster_go<D, G>(s, pdl, p, R);
+      if (e != cudaSuccess || !g_configure_only) return e;
+    }
+  }
+  return attn_go<D, G>(s, pdl, p, R);
+}
+
 template <int D>
 static cudaError_t attn_dim(cudaStream_t s, bool pdl, const AttnParams& p, int R) {
   switch (p.g.heads / p.g.kvh) {
-    case 1: return attn_go<D, 1>(s, pdl, p, R);
-    case 2: return attn_go<D, 2>(s, pdl, p, R);
-    case 3: return attn_go<D, 3>(s, pdl, p, R);
-    case 4: return attn_go<D, 4>(s, pdl, p, R);
-    case 8: return attn_go<D, 8>(s, pdl, p, R);
+    case 1: return attn_dim_go<D, 1>(s, pdl, p, R);
+    case 2: return attn_dim_go<D, 2>(s, pdl, p, R);
+    case 3: return attn_dim_go<D, 3>(s, pdl, p, R);
+    case 4: return attn_dim_go<D, 4>(s, pdl, p, R);
+    case 8: return attn_dim_go<D, 8>(s, pdl, p, R);
   }
   return cudaErrorInvalidValue;
 }
