@@ -942,15 +942,18 @@ cudaError_t encode_forward(Yue2Model& m, cudaStream_t s, int R, bool head, int p
 int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_hint, splits_for(m, R)); }
 
 // Up to kClusterKeys keys over the life of a captured forward (its context plus the positions
-// it will advance), decode passes of up to kMaxRows rows take the cluster form: one 32-key
-// tile per warp of 8-warp CTAs, ceil(tiles / 8) CTAs per (kv head, row), at most
-// kClusterCap (warps then take a second tile). Larger clusters wait for room in one GPC.
-// Measured decode step of the CFG pair (ms; split-K ticket kernel, then clusters of 3..8):
+// it will advance), decode passes of up to kMaxRows rows take the cluster form of attention:
+// 8-warp CTAs with about six 32-key tiles each (one per warp, more CTAs for bandwidth),
+// ceil(tiles / 6) CTAs per (kv head, row), at most kClusterCap (warps then take further tiles
+// one after another). Larger clusters wait for room in one GPC. Measured decode step of the
+// CFG pair (ms; split-K ticket kernel, then clusters of 3..8 CTAs):
 //   1,040 positions: split 1.986, 3: 1.922, 4: 1.916, 5: 1.866, 6: 1.856
-//   1,500: split 1.935, 4: 1.840, 5: 1.850, 6: 1.813, 7 (auto, uncapped): 2.023
+//   1,500: split 1.935, 4: 1.840, 5: 1.850, 6: 1.813, 7: 2.023
 //   1,900: split 1.903, 5: 1.876, 6: 1.857
+//   3,000: split 1.976, 6: 1.908
+//   4,096: split 2.017, 6: 2.020 (the split kernel keeps longer contexts)
 //   2,600: split 1.923, 5: 1.968, 8: 2.120
-constexpr int kClusterKeys = 2048;
+constexpr int kClusterKeys = 3584;
 constexpr int kClusterCap = 6;
 int attn_cluster_for(const Yue2Model& m, int R) {
   if (m.attn_cluster == 0 || m.g.dim > 128 || R > kMaxRows || m.attn_splits > 0) return 0;
@@ -958,7 +961,7 @@ int attn_cluster_for(const Yue2Model& m, int R) {
   const int keys = m.ctx_hint + m.ctx_growth;
   if (keys > kClusterKeys) return 0;
   const int tiles = (keys + 31) / 32;
-  return std::max(1, std::min(kClusterCap, (tiles + kClusterWarps - 1) / kClusterWarps));
+  return std::max(1, std::min(kClusterCap, (tiles + 5) / 6));
 }
 
 int kernels_per_step(const Yue2Model& m, bool head, int phase, int R) {
