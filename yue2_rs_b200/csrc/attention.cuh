@@ -512,9 +512,10 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
 
 // ---- Cluster form for short decode contexts (fused decode rows, D <= 128). The CS CTAs of
 // one (kv head, row) form a thread-block cluster; CTA rank c owns the 32-key tiles
-// [c * TPC, min(ntiles, (c + 1) * TPC)), TPC = ceil(ntiles / CS), one per warp (warps loop
-// when TPC exceeds the warp count). Every tile is requested before griddepcontrol.wait,
-// the one holding the new position without that key: the CTA that computes the new K and V
+// [c * TPC, min(ntiles, (c + 1) * TPC)), TPC = ceil(ntiles / CS), warp w the tiles w, w + 8,
+// ... of them. Each warp's first tile is requested before griddepcontrol.wait; a later
+// tile's K streams in during the previous tile's P.V and its V during its own scores. The
+// tile holding the new position is fetched without that key: the CTA that computes the new K and V
 // (QK norm, RoPE) appends them to the cache and also writes them into its shared-memory
 // tile, so nothing in the launch reads them back from memory. Warps merge in shared memory,
 // then, after a cluster barrier, CTA c merges outputs [c * G * D / CS, ...) of the CS
@@ -566,7 +567,9 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
   const size_t koff = kv_offset(geo, a.layer, 0, g), voff = kv_offset(geo, a.layer, 1, g);
   uint16_t* kt = ktile + warp * 32 * D;
   uint16_t* vt = vtile + warp * 32 * D;
-  auto stage = [&](int t) {  // the tile's keys below the new position (earlier steps wrote them)
+  // the tile's keys below the new position (earlier steps wrote them): K (XOR-swizzled rows)
+  // and V as one group (the first tile) or as two (later tiles, so that K can come early)
+  auto stage_part = [&](int t, bool k, bool v) {
     const int key0 = t << 5;
     const int nk = min(32, pos - key0);
     const uint16_t* page = reinterpret_cast<const uint16_t*>(row.pages[key0 >> kPageLog2]);
@@ -575,12 +578,13 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
     for (int i = lane; i < 32 * CPR; i += 32) {
       const int j = i / CPR, c = i % CPR;
       if (j < nk) {
-        cp_async16(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
-        cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
+        if (k) cp_async16(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8, kb + (size_t)j * D + c * 8);
+        if (v) cp_async16(vt + (size_t)i * 8, vb + (size_t)j * D + c * 8);
       }
     }
     cp_async_commit();
   };
+  auto stage = [&](int t) { stage_part(t, true, true); };
   if (t0 + warp < t1) stage(t0 + warp);
 
   pdl_wait();
@@ -628,23 +632,25 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
     for (int e = 0; e < DL; ++e) acc[h][e] = 0.f;
   }
   float* pw = ps + warp * G * 32;
+  // Warps with several tiles: K of the next tile is requested once the scores no longer need
+  // the K buffer, and its V once P.V is done with the V buffer, so each load overlaps the
+  // other half of the work. Commit groups in flight at the top of iteration it >= 1: K(t),
+  // then V(t).
   for (int t = t0 + warp, it = 0; t < t1; t += NW, ++it) {
     const int key0 = t << 5;
     const int nk = min(32, keys - key0);
-    if (it > 0) stage(t);  // the warp's buffers are free again (end-of-iteration __syncwarp)
-    cp_async_wait<0>();
+    const bool pos_tile = pos - key0 < 32, more = t + NW < t1;
+    const int j_new = pos - key0;  // the new position's row in the pos tile
+    if (it == 0) cp_async_wait<0>();
+    else cp_async_wait<1>();  // K(t); V(t) may still be in flight
     __syncwarp();
-    if (pos - key0 < 32) {  // the new position: its K and V from shared memory
-      const int j = pos - key0;
+    if (pos_tile) {  // the new position's K from shared memory
       for (int c = lane; c < CPR; c += 32) {
-        uint32_t kw[4], vw[4];
+        uint32_t kw[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          kw[e] = pack_bf16x2(knew[c * 8 + 2 * e], knew[c * 8 + 2 * e + 1]);
-          vw[e] = pack_bf16x2(vnew[c * 8 + 2 * e], vnew[c * 8 + 2 * e + 1]);
-        }
-        *reinterpret_cast<uint4*>(kt + (size_t)(j * CPR + (c ^ (j & 7))) * 8) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-        *reinterpret_cast<uint4*>(vt + (size_t)j * D + c * 8) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        for (int e = 0; e < 4; ++e) kw[e] = pack_bf16x2(knew[c * 8 + 2 * e], knew[c * 8 + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(kt + (size_t)(j_new * CPR + (c ^ (j_new & 7))) * 8) =
+            make_uint4(kw[0], kw[1], kw[2], kw[3]);
       }
       __syncwarp();
     }
@@ -674,6 +680,8 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
         }
       }
     }
+    __syncwarp();  // every lane is done with K(t)
+    if (more) stage_part(t + NW, true, false);
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float s = lane < nk ? sc[h] * a.scale : -INFINITY;
@@ -686,7 +694,20 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
 #pragma unroll
       for (int e = 0; e < DL; ++e) acc[h][e] *= alpha;
     }
+    if (it > 0) {  // V(t): the group before K(t + NW)
+      if (more) cp_async_wait<1>();
+      else cp_async_wait<0>();
+    }
     __syncwarp();
+    if (pos_tile) {  // the new position's V from shared memory
+      for (int c = lane; c < CPR; c += 32) {
+        uint32_t vw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vw[e] = pack_bf16x2(vnew[c * 8 + 2 * e], vnew[c * 8 + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(vt + (size_t)j_new * D + c * 8) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      }
+      __syncwarp();
+    }
     for (int j = 0; j < nk; ++j) {
       const uint16_t* vr = vt + (size_t)j * D + lane * DL;
       float vv[DL];
@@ -708,8 +729,10 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
         for (int e = 0; e < DL; ++e) acc[h][e] = fmaf(pj, vv[e], acc[h][e]);
       }
     }
-    __syncwarp();
+    __syncwarp();  // every lane is done with V(t) and the probabilities
+    if (more) stage_part(t + NW, false, true);
   }
+  cp_async_wait<0>();
 
   // ---- this CTA's partial: warps merged in shared memory (tiles reused as accumulators)
   __syncthreads();

@@ -944,16 +944,15 @@ int attn_pipe_for(const Yue2Model& m, int R) { return attn_pipe_for_keys(m.ctx_h
 // Up to kClusterKeys keys over the life of a captured forward (its context plus the positions
 // it will advance), decode passes of up to kMaxRows rows take the cluster form of attention:
 // 8-warp CTAs with about six 32-key tiles each (one per warp, more CTAs for bandwidth),
-// ceil(tiles / 6) CTAs per (kv head, row), at most kClusterCap (warps then take further tiles
-// one after another). Larger clusters wait for room in one GPC. Measured decode step of the
-// CFG pair (ms; split-K ticket kernel, then clusters of 3..8 CTAs):
-//   1,040 positions: split 1.986, 3: 1.922, 4: 1.916, 5: 1.866, 6: 1.856
+// ceil(tiles / 6) CTAs per (kv head, row), at most kClusterCap (warps then stream further
+// tiles, each K during the previous P.V). Larger clusters wait for room in one GPC.
+// Measured decode step of the CFG pair (ms; split-K ticket kernel, then clusters of N CTAs):
+//   1,040 positions: split 1.986, 3: 1.922, 4: 1.916, 5: 1.866, 6: 1.856 (1.840 pipelined)
 //   1,500: split 1.935, 4: 1.840, 5: 1.850, 6: 1.813, 7: 2.023
-//   1,900: split 1.903, 5: 1.876, 6: 1.857
-//   3,000: split 1.976, 6: 1.908
-//   4,096: split 2.017, 6: 2.020 (the split kernel keeps longer contexts)
-//   2,600: split 1.923, 5: 1.968, 8: 2.120
-constexpr int kClusterKeys = 3584;
+//   2,600: split 1.925, 6: 1.851; 3,500: split 2.009, 6: 1.928
+//   4,096: split 2.022, 6: 1.964; 6,000: split 2.124, 6: 2.065
+//   8,192: split 2.169, 6: 2.199 (the split kernel keeps longer contexts)
+constexpr int kClusterKeys = 7168;
 constexpr int kClusterCap = 6;
 int attn_cluster_for(const Yue2Model& m, int R) {
   if (m.attn_cluster == 0 || m.g.dim > 128 || R > kMaxRows || m.attn_splits > 0) return 0;
