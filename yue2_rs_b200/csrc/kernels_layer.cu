@@ -186,6 +186,21 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
     cp_async_wait<0>();
     return;
   }
+  // kEpiResidual, kEpiTpReduce: the residual values this thread's epilogue updates, requested
+  // now so that their round trip overlaps the staging and the stream (only this CTA writes them)
+  constexpr int kPreRes = 2;
+  float res_pre[kPreRes];
+  if (EPI == kEpiResidual || EPI == kEpiTpReduce) {
+#pragma unroll
+    for (int k = 0; k < kPreRes; ++k) {
+      const int i = tid + k * NT;
+      if (i < (row_end - row_begin) * RM && i % RM < p.R) {
+        const int n = row_begin + i / RM;
+        const int sg = (n >= p.seg_start[2]) ? 2 : (n >= p.seg_start[1]) ? 1 : 0;
+        res_pre[k] = p.of[(size_t)(i % RM) * p.ldo + p.col0[sg] + (n - p.seg_start[sg])];
+      }
+    }
+  }
 
   // ---- stage activations
   if (XM == kXF32) {
@@ -298,7 +313,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
       float s = 0.f;
       for (int q = 0; q < p.tp_world; ++q) s += wait_ll(mine + (size_t)q * slot + (size_t)r * p.N + n, tag, p.error, ok);
       float* xr = p.of + (size_t)r * p.ldo + n;
-      *xr = round_bf16(*xr + round_bf16(s));
+      const int k = (i - tid) / NT;  // which of this thread's items (kPreRes == 2)
+      const float xv = k == 0 ? res_pre[0] : k == 1 ? res_pre[1] : *xr;
+      *xr = round_bf16(xv + round_bf16(s));
     }
     return;
   }
@@ -321,7 +338,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams 
       p.ob[(size_t)r * p.ldo + col] = f2bf_round(v[0]);
     } else if (EPI == kEpiResidual) {
       float* xr = p.of + (size_t)r * p.ldo + col;
-      *xr = round_bf16(*xr + round_bf16(v[0]));
+      const int k = (i - tid) / NT;  // which of this thread's items (kPreRes == 2)
+      const float xv = k == 0 ? res_pre[0] : k == 1 ? res_pre[1] : *xr;
+      *xr = round_bf16(xv + round_bf16(v[0]));
     } else if (EPI == kEpiSwiGLU) {
       const float g = round_bf16(v[0]);
       const float u = round_bf16(v[NP - 1]);
