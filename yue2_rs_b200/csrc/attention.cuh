@@ -529,7 +529,8 @@ __host__ __device__ constexpr int attn_cluster_smem() {
          + 2 * kClusterWarps * G * 4          // warp maxima and sums
          + kClusterWarps * D * 4              // norm/rope scratch per warp
          + 2 * D * 4                          // the new position's K and V
-         + G * (D + 2) * 4;                   // this CTA's partial (read by the cluster)
+         + G * (D + 2) * 4                    // this CTA's partial (read by the cluster)
+         + 3 * D * 4;                         // q and k norm gains, the position's cos | sin
 }
 
 template <int D, int G>
@@ -546,6 +547,9 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
   float* knew = wbuf_all + NW * D;                            // [D]
   float* vnew = knew + D;                                     // [D]
   float* cpart = vnew + D;                                    // [G][D + 2]: M, L, O[D]
+  float* gq = cpart + G * (D + 2);                            // [D] q norm gains
+  float* gk = gq + D;                                         // [D] k norm gains
+  float* cs = gk + D;                                         // [D / 2] cos, [D / 2] sin at `pos`
   float* wacc = reinterpret_cast<float*>(smem_raw);           // [NW][G][D] once the tiles are used
 
   cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
@@ -586,17 +590,25 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
   };
   auto stage = [&](int t) { stage_part(t, true, true); };
   if (t0 + warp < t1) stage(t0 + warp);
+  // the norm gains and the RoPE row of `pos` do not depend on the preceding kernel: into
+  // shared memory now, so that the QK norm + RoPE after the wait waits on q alone
+  for (int i = threadIdx.x; i < D; i += NW * 32) {
+    gq[i] = a.q_norm[i];
+    gk[i] = a.k_norm[i];
+    cs[i] = i < D / 2 ? a.cos_tab[(size_t)pos * (D / 2) + i] : a.sin_tab[(size_t)pos * (D / 2) + i - D / 2];
+  }
+  __syncthreads();
 
   pdl_wait();
   pdl_trigger();
 
   const int width = (geo.heads + 2 * geo.kvh) * D;
   const uint16_t* src = a.qkv + (size_t)r * width;
-  const float* ct = a.cos_tab + (size_t)pos * (D / 2);
-  const float* st = a.sin_tab + (size_t)pos * (D / 2);
+  const float* ct = cs;
+  const float* st = cs + D / 2;
   float* wbuf = wbuf_all + warp * D;
   for (int h = warp; h < G; h += NW) {
-    norm_rope_head<D>(src + (size_t)(g * G + h) * D, a.q_norm, geo.eps, ct, st, wbuf);
+    norm_rope_head<D>(src + (size_t)(g * G + h) * D, gq, geo.eps, ct, st, wbuf);
     for (int i = lane; i < D; i += 32) qs[h * D + i] = wbuf[i];
     __syncwarp();
   }
@@ -605,7 +617,7 @@ Y2_DEV void attn_cluster_item(const AttnParams& a, unsigned char* smem_raw) {
     uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
     const size_t slot = (size_t)(pos & (kPageTokens - 1)) * D;
     if (warp == kw) {
-      norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, a.k_norm, geo.eps, ct, st, wbuf);
+      norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, gk, geo.eps, ct, st, wbuf);
       uint16_t* dst = page + koff + slot;
       for (int i = lane; i < D; i += 32) {
         dst[i] = f2bf_exact(wbuf[i]);
