@@ -1091,6 +1091,8 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
     dr[r].advance = 1;
   }
   const float* out = m->logits;
+  m->ctx_hint = 0;  // picks the attention form of this forward
+  for (uint64_t r = 0; r < rows; ++r) m->ctx_hint = std::max(m->ctx_hint, (int)caches[r]->length + 1);
   if (rows >= (uint64_t)m->wide_min && m->tp_world == 1) {  // the GEMM path (gemm_rows.cu)
     if ((rc = ensure_wide(*m))) return rc;
     CK(cudaMemcpyAsync(m->wide_rows, dr.data(), rows * sizeof(DevRow), cudaMemcpyHostToDevice, m->stream));
@@ -1098,8 +1100,6 @@ int yue2_forward(Yue2Model* m, Yue2Cache* const* caches, const int64_t* ids, uin
     out = m->wide_logits;
   } else {
     if ((rc = upload_rows(*m, dr))) return rc;
-    m->ctx_hint = 0;
-    for (uint64_t r = 0; r < rows; ++r) m->ctx_hint = std::max(m->ctx_hint, (int)caches[r]->length + 1);
     if ((rc = run_forward(*m, (int)rows, true, phase))) return rc;
   }
   if (logits) CK(cudaMemcpyAsync(logits, out, rows * m->g.vocab * 4, cudaMemcpyDeviceToHost, m->stream));

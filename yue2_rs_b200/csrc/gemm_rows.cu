@@ -372,6 +372,14 @@ static int row_attention(Yue2Model& m, PrefillBufs& P, DevRow* rows, int l, int 
   ap.max_pos = m.max_pos;
   ap.error = m.flags + 1;
   ap.pipe = fused ? 1 : 0;  // decode rows of the GEMM path: the pipelined tensor-core loop
+  if (fused && R <= 8) {
+    // the cluster form where the rows' contexts allow it (attn_cluster_for), with no more
+    // CTAs per (kv head, row) than leave one wave of them on the SMs. Measured ms/step at a
+    // ~1,040-position context, cluster form against split-K: 4 rows 2.260 / 2.374, 8 rows
+    // 2.368 / 2.398, 16 rows 2.639 / 2.592 (so 16 rows keep the split-K loop)
+    const int cs = attn_cluster_for(m, R);
+    ap.cluster = m.attn_cluster > 0 ? cs : std::min(cs, std::max(1, m.sms / (g.kvh * R)));
+  }
   CK(launch_attention(m.stream, m.wide_pdl, ap, R));
   return 0;
 }
