@@ -592,7 +592,7 @@ def main():
         "gpu_launches": kps * K,
         "clocks": clk,
         "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s", "frac": kern_gbs / peak,
-                     "traffic": traffic, "kernel": "gemv gate|up + SwiGLU, 2 rows (CFG), 100.7 MB per launch",
+                     "traffic": traffic, "kernel": "gemv gate|up + SwiGLU, 2 rows (CFG), 100.7 MB per launch; launches back to back over the 28 layers as programmatic dependents, as in the decode chain",
                      "peak_kind": peak_kind},
         "step_roofline": {"step_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
                           "frac_of_measured": step_bytes / (ms / K * 1e-3) / 1e9 / peak,

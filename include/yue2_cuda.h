@@ -339,8 +339,9 @@ void yue2_session_free(Yue2Session* ss);
 /* Measurement hook (no reference counterpart): `launches` back-to-back launches of one
  * weight-streaming GEMV kind over the layers in turn, `rows` activation rows, CUDA
  * events on the model's stream. kind 0 = gate|up + SwiGLU, 1 = q|k|v, 2 = down +
- * residual, 3 = final norm + LM head, 4 = o + residual. Returns the mean launch time and the weight
- * bytes one launch streams. */
+ * residual, 3 = final norm + LM head, 4 = o + residual. The launches are programmatic dependents
+ * of each other when the model uses them, as in the decode chain. Returns the mean launch time and
+ * the weight bytes one launch streams. */
 int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, double* avg_ms, double* bytes);
 
 #ifdef __cplusplus

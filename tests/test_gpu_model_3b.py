@@ -7,12 +7,14 @@ path (src/model.rs:523-591, src/model.rs:465-468) on bit-identical weights and K
 
   * short context (~300 positions after a GEMM prefill): the SIMT split-K attention;
   * long context (KV filled with seeded N(0,1) bf16 to 4,097 and 24,560 positions, the
-    same values written into the oracle's caches): the pipelined tensor-core attention
-    (attn_mma_kernel) that the engine picks for two rows at these lengths;
+    same values written into the oracle's caches): at 4,097 the cluster form of attention
+    that the engine picks there, and with the cluster form turned off the pipelined
+    tensor-core split-K loop (attn_mma_kernel) that also serves 24,560;
   * BASELINE's initialisation (every weight N(0, 0.02)) at the north_star tolerance,
     and unit-mean RMSNorm gains (logits of order one) at the noise-floor criterion.
 """
 import copy
+import os
 
 import numpy as np
 import pytest
@@ -99,10 +101,19 @@ def test_short_context_two_rows_baseline_init(rng_ids):
         orcm.close()
 
 
-@pytest.mark.parametrize("length", [4097, 24560])
-def test_long_context_two_rows_pipelined_attention(rng_ids, length):
+@pytest.mark.parametrize("length,cluster", [(4097, None), (4097, "0"), (24560, None)])
+def test_long_context_two_rows_pipelined_attention(rng_ids, length, cluster):
     _, _, teacher = rng_ids
-    cfg, dev, orcm = _models(0.0)
+    old = os.environ.get("YUE2_CUDA_ATTN_CLUSTER")
+    if cluster is not None:
+        os.environ["YUE2_CUDA_ATTN_CLUSTER"] = cluster
+    try:
+        cfg, dev, orcm = _models(0.0)
+    finally:
+        if old is None:
+            os.environ.pop("YUE2_CUDA_ATTN_CLUSTER", None)
+        else:
+            os.environ["YUE2_CUDA_ATTN_CLUSTER"] = old
     try:
         assert pipelined_for(length + 1, 2, cfg.num_key_value_heads)
         dcs = [dev.new_cache(length + 4) for _ in range(2)]

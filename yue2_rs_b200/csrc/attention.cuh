@@ -70,6 +70,9 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   float* wm = ps + NW * G * 32;                                        // [NW][G]
   float* wl = wm + NW * G;                                             // [NW][G]
   float* wbuf_all = wl + NW * G;                                       // [NW][D] norm/rope scratch
+  float* gq = wbuf_all + NW * D;                                       // [D] q norm gains (fused)
+  float* gk = gq + D;                                                  // [D] k norm gains
+  float* cs = gk + D;                                                  // [D / 2] cos, [D / 2] sin at pos
   __shared__ int s_ticket;
 
   // Row descriptors are final once the preceding kernel has passed its own wait (it
@@ -146,6 +149,16 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
   }
 
+  // fused rows: the norm gains and the RoPE row of the new position do not depend on the
+  // preceding kernel, so they are staged now and the QK norm after the wait waits on q alone
+  if (a.fused && row.pos >= 0 && row.pos < a.max_pos)
+    for (int i = threadIdx.x; i < D; i += 128) {
+      gq[i] = a.q_norm[i];
+      gk[i] = a.k_norm[i];
+      cs[i] = i < D / 2 ? a.cos_tab[(size_t)row.pos * (D / 2) + i] : a.sin_tab[(size_t)row.pos * (D / 2) + i - D / 2];
+    }
+  attn_sync();
+
   pdl_wait();
   pdl_trigger();
 
@@ -158,11 +171,11 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
     }
     const int width = (geo.heads + 2 * geo.kvh) * D;
     const uint16_t* src = a.qkv + (size_t)r * width;
-    const float* ct = a.cos_tab + (size_t)pos * (D / 2);
-    const float* st = a.sin_tab + (size_t)pos * (D / 2);
+    const float* ct = cs;
+    const float* st = cs + D / 2;
     float* wbuf = wbuf_all + warp * D;
     for (int h = warp; h < G; h += 4) {
-      norm_rope_head<D>(src + (size_t)(g * G + h) * D, a.q_norm, geo.eps, ct, st, wbuf);
+      norm_rope_head<D>(src + (size_t)(g * G + h) * D, gq, geo.eps, ct, st, wbuf);
       for (int i = lane; i < D; i += 32) qs[h * D + i] = wbuf[i];
       __syncwarp();
     }
@@ -170,7 +183,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
       uint16_t* page = reinterpret_cast<uint16_t*>(row.pages[pos >> kPageLog2]);
       const size_t slot = (size_t)(pos & (kPageTokens - 1)) * D;
       if (warp == 0) {
-        norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, a.k_norm, geo.eps, ct, st, wbuf);
+        norm_rope_head<D>(src + (size_t)(geo.heads + g) * D, gk, geo.eps, ct, st, wbuf);
         uint16_t* dst = page + kv_offset(geo, a.layer, 0, g) + slot;
         for (int i = lane; i < D; i += 32) dst[i] = f2bf_exact(wbuf[i]);
       } else if (warp == 1) {
@@ -190,7 +203,7 @@ Y2_DEV void attn_item(const AttnParams& a, int split, int g, int r, unsigned cha
   if constexpr (MMA) {
     constexpr int KS = D / 16, NT = D / 8;
     auto sw = [](int rr, int c) { return (uint32_t)(rr * D * 2 + ((c ^ (rr & 7)) << 4)); };
-    unsigned char* qsb = reinterpret_cast<unsigned char*>(wbuf_all + NW * D);  // [16][D] bf16
+    unsigned char* qsb = reinterpret_cast<unsigned char*>(cs + D);  // [16][D] bf16
     for (int i = threadIdx.x; i < 16 * CPR; i += 128) {
       const int rr = i / CPR, c = i % CPR;
       uint32_t w[4] = {0u, 0u, 0u, 0u};

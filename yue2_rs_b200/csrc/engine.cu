@@ -1157,6 +1157,9 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
   CK(launch_fill_f32(m->stream, m->x, (size_t)kMaxRows * H, 0.5f));
   CK(cudaMemsetAsync(m->attn, 0, (size_t)kMaxRows * qd * 2, m->stream));
   CK(cudaMemsetAsync(m->hbuf, 0, (size_t)kMaxRows * I * 2, m->stream));
+  // launched as the decode chain launches them: programmatic dependents when the model uses
+  // them, so one launch's ramp overlaps the previous launch's tail as it does in a step
+  const bool pdl = m->use_pdl;
   auto one = [&](int layer) -> cudaError_t {
     const LayerW& w = m->layers[layer];
     GemvParams p = {};
@@ -1173,7 +1176,7 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
         p.gamma = w.post_norm;
         p.ob = m->hbuf;
         p.ldo = I;
-        return launch_gemv(m->stream, false, kXNorm, kEpiSwiGLU, p, m->gemv_grid);
+        return launch_gemv(m->stream, pdl, kXNorm, kEpiSwiGLU, p, m->gemv_grid);
       case 1:  // q|k|v
         p.w[0] = w.q;
         p.w[1] = w.k;
@@ -1188,7 +1191,7 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
         p.gamma = w.in_norm;
         p.ob = m->qkv;
         p.ldo = p.N;
-        return launch_gemv(m->stream, false, kXNorm, kEpiBf16, p, m->gemv_grid);
+        return launch_gemv(m->stream, pdl, kXNorm, kEpiBf16, p, m->gemv_grid);
       case 2:  // down + residual
         p.w[0] = p.w[1] = p.w[2] = w.down;
         p.seg_start[1] = p.seg_start[2] = p.N = H;
@@ -1196,7 +1199,7 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
         p.xb = m->hbuf;
         p.of = m->x;
         p.ldo = H;
-        return launch_gemv(m->stream, false, kXBf16, kEpiResidual, p, m->gemv_grid);
+        return launch_gemv(m->stream, pdl, kXBf16, kEpiResidual, p, m->gemv_grid);
       case 4:  // o + residual
         p.w[0] = p.w[1] = p.w[2] = w.o;
         p.seg_start[1] = p.seg_start[2] = p.N = H;
@@ -1204,9 +1207,9 @@ extern "C" int yue2_bench_gemv(Yue2Model* m, int kind, int rows, int launches, d
         p.xb = m->attn;
         p.of = m->x;
         p.ldo = H;
-        return launch_gemv(m->stream, false, kXBf16, kEpiResidual, p, m->gemv_grid);
+        return launch_gemv(m->stream, pdl, kXBf16, kEpiResidual, p, m->gemv_grid);
       default:  // LM head
-        return encode_head(*m, m->stream, false, 0, rows, 0, kPhaseVocab, nullptr);
+        return encode_head(*m, m->stream, pdl, 0, rows, 0, kPhaseVocab, nullptr);
     }
   };
   const double per_row_bytes = kind == 0 ? 2.0 * I * H * 2 : kind == 1 ? (double)(qd + 2 * kd) * H * 2

@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams a) {
 
 static int attention_smem_need(int dim, int groups, bool pipe = false, bool mma = false) {
   const int tiles = (pipe ? 3 : 2) * 4 * 32 * dim * 2;
-  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim) * 4 + (mma ? 16 * dim * 2 : 0);
+  const int extra = (groups * dim + 4 * groups * 32 + 8 * groups + 4 * dim + 3 * dim) * 4 + (mma ? 16 * dim * 2 : 0);
   const int merge = 4 * groups * dim * 4;
   return (tiles > merge ? tiles : merge) + extra;
 }
