@@ -11,7 +11,9 @@ case runs one cluster size over:
   * more CTAs than tiles (ranks whose partial is empty);
   * more tiles than warps in a CTA (warps that take a second tile after the first).
 Logits must meet the north_star tolerance at every step, and the split-K kernel (cluster
-form off) must agree with the same oracle."""
+form off) must agree with the same oracle. Two cases use head_dim 64 with G = 4, the
+kernel's other tile width: a forced size over tile and page edges, and the engine's own
+choice of size."""
 import copy
 import os
 
@@ -30,11 +32,18 @@ def _config():
     return c
 
 
-def _model(cluster):
+def _config_d64():
+    """head_dim 64 and G = 4 (16 query / 4 KV heads), the cluster kernel's other tile width."""
+    return synth.Config(hidden_size=1024, num_hidden_layers=2, num_attention_heads=16, num_key_value_heads=4,
+                        head_dim=64, intermediate_size=2048, vocab_size=8192, rms_norm_eps=1e-6,
+                        rope_theta=10000.0, max_position_embeddings=4096, max_latent_frames=4)
+
+
+def _model(cluster, cfg=None):
     old = os.environ.get("YUE2_CUDA_ATTN_CLUSTER")
     os.environ["YUE2_CUDA_ATTN_CLUSTER"] = str(cluster)
     try:
-        cfg = _config()
+        cfg = cfg or _config()
         return cfg, Model.synthetic(cfg, seed=1, std=0.02, norm_mean=0.0, device=0)
     finally:
         if old is None:
@@ -56,9 +65,15 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("cluster,rows,steps", CASES)
-def test_cluster_attention_matches_oracle(cluster, rows, steps):
-    cfg, dev = _model(cluster)
+D64 = [
+    (3, (("prompt", 62), ("prompt", 31)), 4),  # head_dim 64: tile and page edges over three CTAs
+    (-1, (("fill", 700), ("fill", 650)), 3),   # the engine's own choice of cluster size
+]
+
+
+@pytest.mark.parametrize("cluster,rows,steps,d64", [c + (False,) for c in CASES] + [c + (True,) for c in D64])
+def test_cluster_attention_matches_oracle(cluster, rows, steps, d64):
+    cfg, dev = _model(cluster, _config_d64() if d64 else None)
     orcm = oracle_from_device(dev, cfg)
     try:
         rng = np.random.default_rng(cluster * 31 + rows[0][1])
